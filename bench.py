@@ -1,0 +1,358 @@
+"""Benchmark of the B200 NVFP4 MoE layer (one JSON line on rank 0).
+
+Default workload (N=1): the DeepSeek-V3-shaped decode layer (configuration 2: T=1, H=7168, I=2048, E=256,
+top-8), HBM-bound.  ``--config prefill`` runs configuration 3 (T=4096, biased router), ``--config qwen:T`` the
+Qwen3-30B-A3B shape.  A step is one full layer (router + experts + combine) over one batch.
+
+* ``value``: tokens/s over all ranks, inputs resident in HBM, CUDA events on the launching stream, max over ranks.
+  Weights are 6.3 GB resident (>> 126 MB L2) and every step uses a different input from a pool of 64, so each
+  step streams experts that the previous steps did not touch.
+* ``e2e``: the same metric through the public API with pinned HOST inputs: every step copies x and the router
+  logits host->device, runs the layer and copies the output device->host.
+* ``roofline``: the experts kernel (``skinny_kernel``), timed alone with events around its launch:
+  algorithmic bytes = distinct experts touched x (FP4 codes + E4M3 scales + global scales) + x + out.
+* ``cpu_baseline``: the CPU oracle (a torch/numpy fp32 restatement of the layer; the reference has no CPU
+  implementation) on the host cores, on a bounded sample (one token for decode).
+* ``--impl reference``: times that same CPU restatement per step (the reference arm; rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    "decode": dict(workload="deepseek_v3_moe_decode", E=256, H=7168, I=2048, T=1, k=8, bias_std=0.0),
+    "prefill": dict(workload="deepseek_v3_moe_prefill", E=256, H=7168, I=2048, T=4096, k=8, bias_std=0.5),
+}
+METRIC = "MoE layer tokens/s; decode HBM GB/s & prefill TFLOPS vs B200 roofline"
+
+
+def config_for(name: str) -> dict:
+    if name.startswith("qwen"):
+        T = int(name.split(":")[1]) if ":" in name else 64
+        return dict(workload=f"qwen3_30b_a3b_moe_T{T}", E=128, H=2048, I=768, T=T, k=8, bias_std=0.0)
+    return dict(CONFIGS[name])
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="xcb", choices=["xcb", "reference"])
+    ap.add_argument("--config", default="decode")
+    ap.add_argument("--pool", type=int, default=64)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=1)
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def load_traffic(workload: str):
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        return json.load(open(p)).get(workload)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------------------------- CPU baseline
+def cpu_oracle_sample(weights_dev, x, logits, k, tokens: int):
+    """Time the CPU oracle on the first `tokens` tokens; returns (seconds, tokens, cores)."""
+    import numpy as np
+    import torch
+
+    from oracle import moe_ref
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    xs = x[:tokens]
+    lg = logits[:tokens].float().cpu().numpy()
+    ids, wts = moe_ref.route_topk(lg, k)
+    used = np.unique(ids)
+    sel = torch.as_tensor(used, device=weights_dev["w13"].device)
+    host = {n: weights_dev[n].index_select(0, sel).cpu().numpy() for n in weights_dev}
+    remap = {int(e): i for i, e in enumerate(used)}
+    cid = np.vectorize(remap.get)(ids).astype(np.int32)
+    xb = xs.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    t0 = time.perf_counter()
+    moe_ref.moe_forward(xb, cid, wts, host["w13"], host["w13_sf"], host["w13_gs"], host["w2"], host["w2_sf"],
+                        host["w2_gs"])
+    return time.perf_counter() - t0, tokens, cores
+
+
+# ----------------------------------------------------------------------------------------------- main arm
+def run_xcb(a, cfg, rank, world, dist):
+    import torch
+
+    from xcalibur_b200 import PreparedMoE, synth
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    E, H, I, T, k = cfg["E"], cfg["H"], cfg["I"], cfg["T"], cfg["k"]
+    weights = synth.make_weights(E, H, I, seed=1234, device=dev)
+    layer = PreparedMoE(*weights.values())
+    P = max(1, a.pool if T <= 64 else 2)
+    xs, lgs = [], []
+    for i in range(P):
+        x, lg = synth.make_inputs(T, H, E, seed=1000 * rank + i + 1, device=dev, bias_std=cfg["bias_std"])
+        xs.append(x)
+        lgs.append(lg)
+    outs = [torch.empty((T, H), dtype=torch.bfloat16, device=dev) for _ in range(P)]
+    calls = [layer.build_call(xs[i], lgs[i], k, out=outs[i], return_routing=True) for i in range(P)]
+    torch.cuda.synchronize()
+    # distinct experts per input (for the algorithmic byte count)
+    for c in calls:
+        c.launch()
+    torch.cuda.synchronize()
+    if layer.check_device_status():
+        raise RuntimeError("device status bits set during warm-up")
+    U = [int(torch.unique(c.ids_out).numel()) for c in calls]
+
+    def step(i, ev_a=None, ev_b=None):
+        c = calls[i % P]
+        c.launch("route")
+        if ev_a is not None:
+            ev_a.record()
+        c.launch("experts")
+        if ev_b is not None:
+            ev_b.record()
+
+    for i in range(a.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    K = a.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev.index)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    start.record()
+    for i in range(K):
+        step(i, *ev[i])
+    end.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if dist:
+        dist.barrier()
+    ms = start.elapsed_time(end) / K
+    kern_ms = sum(e_a.elapsed_time(e_b) for e_a, e_b in ev) / K
+    u_avg = sum(U[i % P] for i in range(K)) / K
+    if layer.check_device_status():
+        raise RuntimeError("device status bits set in the timed region")
+
+    # ---- end to end through the public API with pinned host buffers
+    xh = [x.cpu().pin_memory() for x in xs]
+    lh = [l.cpu().pin_memory() for l in lgs]
+    oh = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(xs[0])
+    ld = torch.empty_like(lgs[0])
+    od = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    ecall = layer.build_call(xd, ld, k, out=od)
+
+    def e2e_step(i):
+        xd.copy_(xh[i % P], non_blocking=True)
+        ld.copy_(lh[i % P], non_blocking=True)
+        ecall.launch()
+        oh.copy_(od, non_blocking=True)
+
+    for i in range(a.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(K):
+        e2e_step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / K
+
+    if dist:
+        import torch.distributed as td
+
+        t = torch.tensor([ms, kern_ms, e2e_ms], dtype=torch.float64, device=dev)
+        td.all_reduce(t, op=td.ReduceOp.MAX)
+        ms, kern_ms, e2e_ms = t.tolist()
+
+    hbm, bf16, bf16_sus, src = load_peaks()
+    per_expert = synth.layer_bytes(1, H, I)
+    alg_bytes = u_avg * per_expert + 2 * T * H * 2
+    flops = synth.layer_flops(T, k, H, I)
+    if T <= 256:
+        achieved = alg_bytes / (kern_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4), "peak_source": src}
+    else:
+        achieved = flops / (kern_ms * 1e-3) / 1e12
+        peak = bf16_sus
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "peak_source": src + " (sustained)"}
+    roof["traffic"] = load_traffic(cfg["workload"])
+    roof["kernel"] = "skinny_kernel"
+    roof["kernel_ms"] = round(kern_ms, 5)
+    roof["algorithmic_bytes"] = int(alg_bytes)
+    roof["algorithmic_flops"] = int(flops)
+
+    res = {
+        "metric": METRIC,
+        "value": round(T * world / (ms * 1e-3), 2),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": a.warmup,
+        "ms_per_step": round(ms, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "nvfp4 weights (e2m1 + e4m3 block scales) x bf16 activations, fp32 accumulate",
+        "data": "synthetic: seeded N(0,0.02) weights quantised to NVFP4 on the GPU; bf16 N(0,1) activations; "
+                "fp32 N(0,1) router logits",
+        "config": {"workload": cfg["workload"], "tokens": T, "hidden": H, "inter": I, "experts": E, "top_k": k,
+                   "router_bias_std": cfg["bias_std"], "parallelism": "replicas" if world > 1 else "single",
+                   "l2": f"{P} rotating inputs; 6.3 GB of packed weights resident (>126 MB L2); "
+                         f"{u_avg:.1f} distinct experts per step on average"},
+        "roofline": roof,
+        "e2e": {"value": round(T * world / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * H * 2 + T * E * 4, "d2h_bytes_per_step": T * H * 2},
+        "gpu_launches": 2 * K,
+        "clocks": clk,
+    }
+    if rank == 0 and not a.no_cpu_baseline:
+        secs, n, cores = cpu_oracle_sample(weights, xs[0], lgs[0], k, min(T, a.cpu_sample_tokens))
+        res["cpu_baseline"] = {"value": round(n / secs, 4), "unit": "tokens/s", "cores": cores, "kind": "port",
+                               "sample": f"{n} token(s) of {cfg['workload']} through the CPU oracle "
+                                         f"({secs:.2f} s, dequantise + fp32 matmuls, torch threads={cores})"}
+    return res
+
+
+def run_reference(a, cfg):
+    """Reference arm: the CPU restatement of the layer (the reference has no CPU implementation), per step."""
+    import torch
+
+    from xcalibur_b200 import synth  # noqa: F401  (only for the byte/flop helpers)
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    E, H, I, T, k = cfg["E"], cfg["H"], cfg["I"], cfg["T"], cfg["k"]
+    weights = synth.make_weights(E, H, I, seed=1234, device=dev)
+    x, lg = synth.make_inputs(T, H, E, seed=1, device=dev, bias_std=cfg["bias_std"])
+    n = min(T, a.cpu_sample_tokens)
+    times = []
+    for i in range(a.warmup + a.steps):
+        secs, _, cores = cpu_oracle_sample(weights, x, lg, k, n)
+        if i >= a.warmup:
+            times.append(secs)
+    secs = sum(times) / len(times)
+    val = round(n / secs, 4)
+    return {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": 1, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(secs * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32 (CPU restatement)", "data": "synthetic (same seeds as the main arm)",
+        "config": {"workload": cfg["workload"], "tokens": T, "hidden": H, "inter": I, "experts": E, "top_k": k},
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{n} token(s) per step of {cfg['workload']} through the CPU oracle"},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    a = parse()
+    cfg = config_for(a.config)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if a.impl == "reference":
+        if rank == 0:
+            # reduce the per-step sample so the whole run stays within a few minutes
+            a.steps = min(a.steps, 3)
+            a.warmup = min(a.warmup, 1)
+            print(json.dumps(run_reference(a, cfg)), flush=True)
+        return
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as td
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist = td
+    try:
+        res = run_xcb(a, cfg, rank, world, dist)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        if dist:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,142 @@
+/* C-ABI of the B200 (sm_100a) NVFP4-weight / BF16-activation mixture-of-experts layer.
+ *
+ * Drop-in for the native boundary of xCalibur's kernels/moe_w4a16_h200 operator.  The reference binds one pybind
+ * entry point, okc_run(w, scratch, x, topk_ids, topk_weights, out, lo, nloc, grid) (moe_w4a16.py:2812, declared
+ * at :3063-3068), builds its packed weights in Python in prepare() (moe_w4a16.py:3292-3351) and allocates its
+ * scratch in _make_scratch() (moe_w4a16.py:3353-3367).  Here every argument is a plain device pointer plus sizes,
+ * every call takes an explicit cudaStream_t, and the library never allocates: the caller provides the packed
+ * weight buffers and the workspace, sized by the *_bytes queries.
+ *
+ * All calls return XCB_OK or an XCB_ERR_* code; argument and shape errors are detected on the host before any
+ * launch.  Errors that only the device can see (a NaN block scale, an expert id out of range, a spin-wait that
+ * ran out of time) set bits in a status word inside the workspace; xcb_moe_read_status() reads and clears it.
+ */
+#ifndef XCB_MOE_H_
+#define XCB_MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- return codes ---- */
+#define XCB_OK 0
+#define XCB_ERR_INVALID_ARG 1       /* null pointer, negative size, misaligned pointer, bad flag     */
+#define XCB_ERR_UNSUPPORTED 2       /* shape outside what the kernels support (see xcb_moe_check_shape) */
+#define XCB_ERR_WORKSPACE 3         /* workspace smaller than xcb_moe_workspace_bytes()               */
+#define XCB_ERR_CUDA 4              /* a CUDA runtime call or launch failed                            */
+#define XCB_ERR_DEVICE 5            /* xcb_moe_read_status found device-side status bits               */
+
+/* ---- device status bits (xcb_moe_read_status) ---- */
+#define XCB_STATUS_DEVICE_TIMEOUT 1 /* a bounded spin-wait gave up (the output of that call is invalid) */
+#define XCB_STATUS_BAD_EXPERT 2     /* a topk id outside [0, total_experts): that route was dropped   */
+#define XCB_STATUS_NAN_SCALE 4      /* the packer met a NaN E4M3 block scale                          */
+#define XCB_STATUS_CAPACITY 8       /* more routes than the workspace was sized for                   */
+
+/* ---- forward flags ---- */
+#define XCB_FLAG_POST_NORM 1        /* reference contract: y *= (1 + post_norm_w); out = sum w * y / rms(y) */
+
+/* Shape of one prepared layer.  total_experts is the router width (logits columns, valid topk ids);
+ * experts [expert_offset, expert_offset + num_experts) are held in the packed buffers (the reference's
+ * local_start / local_count, moe_w4a16.py:105-110). */
+typedef struct XcbMoeShape {
+  int32_t num_experts;    /* experts held in the packed buffers                                           */
+  int32_t total_experts;  /* router width                                                                  */
+  int32_t expert_offset;  /* global id of held expert 0                                                    */
+  int32_t hidden;         /* H: x and out row length; K of gate_up; rows of down                           */
+  int32_t inter;          /* I: rows of gate (and of up); K of down                                        */
+} XcbMoeShape;
+
+/* Packed weights (device memory owned by the caller) + per-expert fp32 global scales + optional bf16 post-norm. */
+typedef struct XcbMoeWeights {
+  XcbMoeShape shape;
+  const void* gate_up;        /* xcb_moe_packed_bytes(shape, 0) bytes, written by xcb_moe_pack_weights */
+  const void* down;           /* xcb_moe_packed_bytes(shape, 1) bytes                                   */
+  const float* gate_up_gs;    /* [num_experts]  (reference w13_gs, moe_w4a16.py:72-79)                 */
+  const float* down_gs;       /* [num_experts]  (reference w2_gs)                                       */
+  const uint16_t* post_norm_w;/* bf16 [hidden] or NULL (reference post_norm_w)                          */
+} XcbMoeWeights;
+
+/* One forward call.  Either router_logits (north_star form: softmax -> top-k -> renormalise, ties to the lower
+ * expert id) or topk_ids + topk_weights (reference form, moe_w4a16.py:93-97) must be given. */
+typedef struct XcbMoeArgs {
+  int32_t tokens;                 /* T (0 is allowed: nothing is launched)                      */
+  int32_t top_k;                  /* routes per token, 1..16                                    */
+  int32_t flags;                  /* XCB_FLAG_*                                                 */
+  int32_t reserved;
+  const uint16_t* hidden_states;  /* bf16 [T, hidden], rows 16-byte aligned                     */
+  const float* router_logits;     /* fp32 [T, total_experts] or NULL                            */
+  const int32_t* topk_ids;        /* int32 [T, top_k] global ids, or NULL                       */
+  const float* topk_weights;      /* fp32 [T, top_k], or NULL                                   */
+  uint16_t* out;                  /* bf16 [T, hidden]                                           */
+  int32_t* topk_ids_out;          /* optional int32 [T, top_k]: the routing used                */
+  float* topk_weights_out;        /* optional fp32 [T, top_k]                                   */
+} XcbMoeArgs;
+
+/* Human-readable name of a return code. */
+const char* xcb_status_str(int code);
+
+/* XCB_OK if the kernels support this shape (hidden and inter multiples of 256, hidden <= 8192, ...). */
+int xcb_moe_check_shape(const XcbMoeShape* shape);
+
+/* Bytes of one packed tensor: which = 0 gate_up [E, 2I, H], 1 down [E, H, I].
+ * Replaces the reference's packed copies built in prepare() (moe_w4a16.py:3292-3351). */
+size_t xcb_moe_packed_bytes(const XcbMoeShape* shape, int which);
+
+/* Repack reference-layout NVFP4 weights into the kernels' layout on the GPU (lossless; never requantises).
+ * w13: uint8 [E, 2I, H/2] (gate rows then up rows, low nibble = even k), w13_sf: E4M3 bytes [E, 2I, H/16],
+ * w2: uint8 [E, H, I/2], w2_sf: [E, H, I/16] (moe_w4a16.py:72-79, nibble order :3151-3158); E = shape.num_experts
+ * experts starting at the pointers given.  xor_tables: device uint32 [4*256], the GF(2) packing transform of the
+ * decoder (xcalibur_b200/packer.py).  status: device int32, gets XCB_STATUS_NAN_SCALE on a NaN scale.
+ * Replaces _pack_codes/_pack_scales and the GF(2) word transform (moe_w4a16.py:3168-3190, :3903-3933). */
+int xcb_moe_pack_weights(const XcbMoeShape* shape, const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* w2,
+                         const uint8_t* w2_sf, const uint32_t* xor_tables, void* gate_up_out, void* down_out,
+                         int32_t* status, cudaStream_t stream);
+
+/* Workspace bytes for calls of up to max_tokens tokens with top_k routes each (reference scratch:
+ * _make_scratch, moe_w4a16.py:3353-3367). */
+size_t xcb_moe_workspace_bytes(const XcbMoeShape* shape, int32_t max_tokens, int32_t top_k);
+
+/* Byte offsets of the routing arrays inside a workspace sized for (max_tokens, top_k), for inspection by tests and
+ * callers that want the permutation: out[0] ids int32 [T*k], out[1] weights fp32 [T*k], out[2] pos int32 [T*k]
+ * (permuted position of each flat route, -1 if not local), out[3] order int32 [routes] (flat route at each
+ * permuted position), out[4] counts int32 [num_experts], out[5] offsets int32 [num_experts + 1].
+ * Returns the number of entries written (6) or -1 on bad arguments. */
+int xcb_moe_workspace_offsets(const XcbMoeShape* shape, int32_t max_tokens, int32_t top_k, size_t* out, int n);
+
+/* Zero a fresh workspace (once, before its first forward call).  Calls keep it consistent afterwards. */
+int xcb_moe_workspace_init(void* workspace, size_t bytes, int32_t max_tokens, int32_t top_k, cudaStream_t stream);
+
+/* One MoE layer: out = sum_k w_k * down_e(SiLU(gate_e x) * up_e x) (or the post-norm form with
+ * XCB_FLAG_POST_NORM).  Asynchronous on `stream`; no host synchronisation; graph-capturable.
+ * Replaces okc_run (moe_w4a16.py:2812-2886) and kernel_fn's variant dispatch (moe_w4a16.py:3370-3399).
+ * Calls that share a workspace must be ordered on one stream. */
+int xcb_moe_forward(const XcbMoeWeights* weights, const XcbMoeArgs* args, void* workspace, size_t workspace_bytes,
+                    cudaStream_t stream);
+
+/* The two halves of xcb_moe_forward, for callers that time or schedule them separately: xcb_moe_route runs the
+ * router, the expert histogram and the stable permutation into the workspace; xcb_moe_experts then runs the
+ * expert MLPs and the weighted combine.  They must be called with the same arguments, in this order, on one
+ * stream. */
+int xcb_moe_route(const XcbMoeWeights* weights, const XcbMoeArgs* args, void* workspace, size_t workspace_bytes,
+                  cudaStream_t stream);
+int xcb_moe_experts(const XcbMoeWeights* weights, const XcbMoeArgs* args, void* workspace, size_t workspace_bytes,
+                    cudaStream_t stream);
+
+/* Synchronise `stream`, read the workspace status bits into *device_status, clear them.
+ * Returns XCB_OK if none were set, XCB_ERR_DEVICE otherwise. */
+int xcb_moe_read_status(void* workspace, int32_t* device_status, cudaStream_t stream);
+
+/* Quantise fp32 weights [E, R, K] to NVFP4 (gs = amax/(6*448) per expert, sf = e4m3(block_amax/6/gs),
+ * codes RNE to E2M1): codes [E, R, K/2], sf [E, R, K/16], gs [E].  A utility for synthetic weights; the
+ * reference receives already-quantised weights.  amax_scratch: device float [E] (zeroed by this call). */
+int xcb_nvfp4_quantize(const float* w, int32_t E, int32_t R, int32_t K, uint8_t* codes, uint8_t* sf, float* gs,
+                       float* amax_scratch, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* XCB_MOE_H_ */

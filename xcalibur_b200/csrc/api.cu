@@ -1,0 +1,209 @@
+// extern "C" boundary (include/xcb_moe.h): argument validation, workspace carving, launch sequencing.
+#include <string.h>
+
+#include "common.cuh"
+#include "workspace.cuh"
+
+#include "kernels.cuh"
+
+using namespace xcb;
+
+namespace {
+constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per bounded wait
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+int shape_ok(const XcbMoeShape* s) {
+  if (!s) return XCB_ERR_INVALID_ARG;
+  if (s->num_experts <= 0 || s->total_experts <= 0 || s->hidden <= 0 || s->inter <= 0 || s->expert_offset < 0)
+    return XCB_ERR_INVALID_ARG;
+  if (s->expert_offset + s->num_experts > s->total_experts) return XCB_ERR_INVALID_ARG;
+  if (s->hidden % 256 || s->inter % 256) return XCB_ERR_UNSUPPORTED;
+  if (s->total_experts > 512 || s->num_experts > 512) return XCB_ERR_UNSUPPORTED;
+  if (skinny_smem_bytes(s->hidden, s->inter) > 227 * 1024) return XCB_ERR_UNSUPPORTED;
+  return XCB_OK;
+}
+}  // namespace
+
+extern "C" {
+
+const char* xcb_status_str(int code) {
+  switch (code) {
+    case XCB_OK: return "ok";
+    case XCB_ERR_INVALID_ARG: return "invalid argument";
+    case XCB_ERR_UNSUPPORTED: return "unsupported shape";
+    case XCB_ERR_WORKSPACE: return "workspace too small";
+    case XCB_ERR_CUDA: return "CUDA error";
+    case XCB_ERR_DEVICE: return "device status bits set";
+    default: return "unknown status";
+  }
+}
+
+int xcb_moe_check_shape(const XcbMoeShape* shape) { return shape_ok(shape); }
+
+size_t xcb_moe_packed_bytes(const XcbMoeShape* s, int which) {
+  if (shape_ok(s) != XCB_OK) return 0;
+  const size_t E = (size_t)s->num_experts, H = (size_t)s->hidden, I = (size_t)s->inter;
+  return which == 0 ? E * (2 * I / 16) * 9 * H : E * (H / 16) * 9 * I;
+}
+
+int xcb_moe_pack_weights(const XcbMoeShape* s, const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* w2,
+                         const uint8_t* w2_sf, const uint32_t* xor_tables, void* gate_up_out, void* down_out,
+                         int32_t* status, cudaStream_t stream) {
+  int rc = shape_ok(s);
+  if (rc != XCB_OK) return rc;
+  if (!w13 || !w13_sf || !w2 || !w2_sf || !xor_tables || !gate_up_out || !down_out || !status)
+    return XCB_ERR_INVALID_ARG;
+  if (!aligned16(gate_up_out) || !aligned16(down_out)) return XCB_ERR_INVALID_ARG;
+  PackParams a{w13, w13_sf, (uint8_t*)gate_up_out, xor_tables, status, s->num_experts, 2 * s->inter, s->hidden, 1};
+  rc = launch_pack(a, stream);
+  if (rc != XCB_OK) return rc;
+  PackParams b{w2, w2_sf, (uint8_t*)down_out, xor_tables, status, s->num_experts, s->hidden, s->inter, 0};
+  return launch_pack(b, stream);
+}
+
+size_t xcb_moe_workspace_bytes(const XcbMoeShape* s, int32_t max_tokens, int32_t top_k) {
+  if (shape_ok(s) != XCB_OK || max_tokens < 0 || top_k <= 0) return 0;
+  return ws_layout(s->num_experts, s->hidden, s->inter, max_tokens, top_k).total;
+}
+
+int xcb_moe_workspace_offsets(const XcbMoeShape* s, int32_t max_tokens, int32_t top_k, size_t* out, int n) {
+  if (shape_ok(s) != XCB_OK || max_tokens < 0 || top_k <= 0 || !out || n < 6) return -1;
+  const WsLayout L = ws_layout(s->num_experts, s->hidden, s->inter, max_tokens, top_k);
+  out[0] = L.ids;
+  out[1] = L.wts;
+  out[2] = L.pos;
+  out[3] = L.order;
+  out[4] = L.counts;
+  out[5] = L.offsets;
+  return 6;
+}
+
+int xcb_moe_workspace_init(void* ws, size_t bytes, int32_t max_tokens, int32_t top_k, cudaStream_t stream) {
+  (void)max_tokens;
+  (void)top_k;
+  if (!ws) return XCB_ERR_INVALID_ARG;
+  return cudaMemsetAsync(ws, 0, bytes, stream) == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
+}
+
+namespace {
+// Validate a forward call and carve its workspace; shared by route / experts / forward.
+int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t ws_bytes, RouteParams* rp,
+                 SkinnyParams* sp) {
+  if (!w || !a || !ws) return XCB_ERR_INVALID_ARG;
+  const XcbMoeShape* s = &w->shape;
+  int rc = shape_ok(s);
+  if (rc != XCB_OK) return rc;
+  if (a->tokens < 0 || a->top_k <= 0 || a->top_k > 16 || a->top_k > s->total_experts) return XCB_ERR_INVALID_ARG;
+  if (a->tokens == 0) return XCB_OK;
+  if (!a->hidden_states || !a->out || !w->gate_up || !w->down || !w->gate_up_gs || !w->down_gs)
+    return XCB_ERR_INVALID_ARG;
+  const bool have_logits = a->router_logits != nullptr;
+  const bool have_ids = a->topk_ids != nullptr && a->topk_weights != nullptr;
+  if (have_logits == have_ids) return XCB_ERR_INVALID_ARG;
+  const bool post_norm = (a->flags & XCB_FLAG_POST_NORM) != 0;
+  if (post_norm && !w->post_norm_w) return XCB_ERR_INVALID_ARG;
+  if (a->flags & ~XCB_FLAG_POST_NORM) return XCB_ERR_INVALID_ARG;
+  if (!aligned16(a->hidden_states) || !aligned16(a->out) || !aligned16(w->gate_up) || !aligned16(w->down) ||
+      !aligned16(ws))
+    return XCB_ERR_INVALID_ARG;
+  const WsLayout L = ws_layout(s->num_experts, s->hidden, s->inter, a->tokens, a->top_k);
+  if (ws_bytes < L.total) return XCB_ERR_WORKSPACE;
+  uint8_t* b = (uint8_t*)ws;
+
+  rp->logits = a->router_logits;
+  rp->ids_in = a->topk_ids;
+  rp->wts_in = a->topk_weights;
+  rp->T = a->tokens;
+  rp->k = a->top_k;
+  rp->E_tot = s->total_experts;
+  rp->lo = s->expert_offset;
+  rp->E_loc = s->num_experts;
+  rp->ctl = (int*)(b + L.ctl);
+  rp->ids = (int*)(b + L.ids);
+  rp->wts = (float*)(b + L.wts);
+  rp->pos = (int*)(b + L.pos);
+  rp->order = (int*)(b + L.order);
+  rp->counts = (int*)(b + L.counts);
+  rp->offsets = (int*)(b + L.offsets);
+  rp->jobs = (int4*)(b + L.jobs);
+  rp->doneA = (int*)(b + L.doneA);
+  rp->ss = (float*)(b + L.ss);
+  rp->ids_out = a->topk_ids_out;
+  rp->wts_out = a->topk_weights_out;
+
+  sp->wA = (const uint8_t*)w->gate_up;
+  sp->wB = (const uint8_t*)w->down;
+  sp->gsA = w->gate_up_gs;
+  sp->gsB = w->down_gs;
+  sp->normw = w->post_norm_w;
+  sp->x = a->hidden_states;
+  sp->order = rp->order;
+  sp->wts = rp->wts;
+  sp->pos = rp->pos;
+  sp->jobs = rp->jobs;
+  sp->ctl = rp->ctl;
+  sp->doneA = rp->doneA;
+  sp->inter = (uint16_t*)(b + L.inter);
+  sp->y = (float*)(b + L.y);
+  sp->ss = rp->ss;
+  sp->out = a->out;
+  sp->T = a->tokens;
+  sp->k = a->top_k;
+  sp->H = s->hidden;
+  sp->I = s->inter;
+  sp->post_norm = post_norm ? 1 : 0;
+  sp->timeout_ns = kTimeoutNs;
+  return XCB_OK;
+}
+}  // namespace
+
+int xcb_moe_route(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  RouteParams rp;
+  SkinnyParams sp;
+  int rc = prepare_call(w, a, ws, ws_bytes, &rp, &sp);
+  if (rc != XCB_OK || a->tokens == 0) return rc;
+  return launch_route(rp, stream);
+}
+
+int xcb_moe_experts(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  RouteParams rp;
+  SkinnyParams sp;
+  int rc = prepare_call(w, a, ws, ws_bytes, &rp, &sp);
+  if (rc != XCB_OK || a->tokens == 0) return rc;
+  return launch_skinny(sp, stream);
+}
+
+int xcb_moe_forward(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  RouteParams rp;
+  SkinnyParams sp;
+  int rc = prepare_call(w, a, ws, ws_bytes, &rp, &sp);
+  if (rc != XCB_OK || a->tokens == 0) return rc;
+  rc = launch_route(rp, stream);
+  if (rc != XCB_OK) return rc;
+  return launch_skinny(sp, stream);
+}
+
+int xcb_moe_read_status(void* ws, int32_t* device_status, cudaStream_t stream) {
+  if (!ws || !device_status) return XCB_ERR_INVALID_ARG;
+  int v = 0;
+  if (cudaMemcpyAsync(&v, ws, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess) return XCB_ERR_CUDA;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return XCB_ERR_CUDA;
+  *device_status = v;
+  if (v) {
+    if (cudaMemsetAsync(ws, 0, sizeof(int), stream) != cudaSuccess) return XCB_ERR_CUDA;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return XCB_ERR_CUDA;
+    return XCB_ERR_DEVICE;
+  }
+  return XCB_OK;
+}
+
+int xcb_nvfp4_quantize(const float* w, int32_t E, int32_t R, int32_t K, uint8_t* codes, uint8_t* sf, float* gs,
+                       float* amax_scratch, cudaStream_t stream) {
+  if (!w || !codes || !sf || !gs || !amax_scratch || E <= 0 || R <= 0 || K <= 0 || K % 16) return XCB_ERR_INVALID_ARG;
+  if (!aligned16(w)) return XCB_ERR_INVALID_ARG;
+  QuantParams q{w, E, R, K, codes, sf, gs, amax_scratch};
+  return launch_quantize(q, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,76 @@
+// Parameter blocks and launchers of the kernels behind the C-ABI (one definition, shared by all translation units).
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+namespace xcb {
+
+struct RouteParams {
+  const float* logits;     // [T, E_tot] or null
+  const int* ids_in;       // [T, k] or null
+  const float* wts_in;     // [T, k] or null
+  int T, k, E_tot, lo, E_loc;
+  int* ctl;
+  int* ids;
+  float* wts;
+  int* pos;
+  int* order;
+  int* counts;
+  int* offsets;
+  int4* jobs;
+  int* doneA;              // per-job phase-A counters, zeroed here for the kernel that follows
+  float* ss;
+  int* ids_out;
+  float* wts_out;
+};
+
+struct SkinnyParams {
+  const uint8_t* wA;      // packed gate_up units
+  const uint8_t* wB;      // packed down units
+  const float* gsA;
+  const float* gsB;
+  const uint16_t* normw;  // bf16 [H] or null
+  const uint16_t* x;      // bf16 [T, H]
+  const int* order;       // permuted position -> flat route
+  const float* wts;       // flat route weights
+  const int* pos;         // flat route -> permuted position (-1: not local)
+  const int4* jobs;       // (expert, p0, ntok, 0)
+  int* ctl;
+  int* doneA;
+  uint16_t* inter;        // bf16 [routes, I]
+  float* y;               // fp32 [routes, H]
+  float* ss;              // fp32 [routes]
+  uint16_t* out;          // bf16 [T, H]
+  int T, k, H, I;
+  int post_norm;
+  unsigned long long timeout_ns;
+};
+
+struct PackParams {
+  const uint8_t* codes;  // [E, R, K/2]
+  const uint8_t* sf;     // [E, R, K/16]
+  uint8_t* out;          // [E, R/16, 9K]
+  const uint32_t* tabs;  // [4][256]
+  int* status;
+  int E, R, K;
+  int gate_up;           // rows interleaved gate/up in 8-row groups
+};
+
+struct QuantParams {
+  const float* w;
+  int E, R, K;
+  uint8_t* codes;
+  uint8_t* sf;
+  float* gs;
+  float* amax;
+};
+
+int launch_route(const RouteParams& p, cudaStream_t stream);
+size_t route_smem_bytes(int E_loc);
+int launch_skinny(const SkinnyParams& p, cudaStream_t stream);
+size_t skinny_smem_bytes(int H, int I);
+int launch_pack(const PackParams& p, cudaStream_t stream);
+int launch_quantize(const QuantParams& p, cudaStream_t stream);
+
+}  // namespace xcb

@@ -1,0 +1,59 @@
+// Workspace layout shared by the host launcher and the kernels.  The caller allocates xcb_moe_workspace_bytes()
+// and zeroes it once (xcb_moe_workspace_init).  The control words sit at offset 0 whatever the call's size; the
+// kernel that uses them returns them to zero before it exits.  Every other region is rewritten by each call
+// before it is read (the router zeroes the per-job counters), so consecutive calls of any size on one stream
+// need no host-side reset and stay graph-capturable.
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+namespace xcb {
+
+constexpr int kJobTokens = 8;  // tokens per decode-path job (one m16n8k16 n-tile)
+
+// Control words at the start of the workspace.
+enum CtlWord : int {
+  kCtlStatus = 0,      // XCB_STATUS_* bits
+  kCtlGridArrive = 1,  // grid barrier of the decode-path kernel
+  kCtlExit = 2,        // CTAs that finished the decode-path kernel (the last one resets the counters)
+  kCtlJobs = 3,        // number of jobs written by the router
+  kCtlRoutes = 4,      // number of local routes
+  kCtlWords = 64
+};
+
+struct WsLayout {
+  size_t ctl, ids, wts, pos, order, counts, offsets, jobs, doneA, ss, inter, y, total;
+  int max_routes, max_jobs;
+};
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+inline WsLayout ws_layout(int E_loc, int H, int I, int max_tokens, int top_k) {
+  WsLayout L;
+  const size_t R = (size_t)max_tokens * (size_t)top_k;
+  L.max_routes = (int)R;
+  const size_t ej = (size_t)E_loc < R ? (size_t)E_loc : R;
+  L.max_jobs = (int)(R / kJobTokens + ej + 1);
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = o;
+    o = align_up(o + bytes, 256);
+    return at;
+  };
+  L.ctl = take(kCtlWords * 4);
+  L.ids = take(R * 4);
+  L.wts = take(R * 4);
+  L.pos = take(R * 4);
+  L.order = take(R * 4);
+  L.counts = take((size_t)E_loc * 4);
+  L.offsets = take(((size_t)E_loc + 1) * 4);
+  L.jobs = take((size_t)L.max_jobs * 16);
+  L.doneA = take((size_t)L.max_jobs * 4);
+  L.ss = take(R * 4);
+  L.inter = take(R * (size_t)I * 2);
+  L.y = take(R * (size_t)H * 4);
+  L.total = o;
+  return L;
+}
+
+}  // namespace xcb
