@@ -126,6 +126,21 @@ int xcb_moe_route(const XcbMoeWeights* weights, const XcbMoeArgs* args, void* wo
 int xcb_moe_experts(const XcbMoeWeights* weights, const XcbMoeArgs* args, void* workspace, size_t workspace_bytes,
                     cudaStream_t stream);
 
+/* Size of the fixed scratch behind xcb_moe_forward_static (8 MiB, reserved on every GPU that loads the library). */
+#define XCB_STATIC_SCRATCH_BYTES (8u << 20)
+
+/* xcb_moe_forward without a caller-provided workspace, for callers that cannot allocate device memory: a host
+ * framework that owns every device byte through its own allocator and forbids plugins to call cudaMalloc, or a
+ * latency-critical decode loop where cudaMalloc/cudaFree would stall or synchronise the device.  No counterpart in
+ * the reference (its scratch is always allocated by prepare(), moe_w4a16.py:3353-3367).
+ * The scratch is one file-scope device array of XCB_STATIC_SCRATCH_BYTES per GPU, held until the process exits;
+ * a call whose workspace would exceed it (xcb_moe_workspace_bytes(shape, tokens, top_k) > XCB_STATIC_SCRATCH_BYTES,
+ * e.g. more than 31 tokens x top-8 at the DeepSeek-V3 shape) returns XCB_ERR_WORKSPACE before any launch.  The
+ * function allocates nothing.  Its first call on a device looks up the array's device address (with that device
+ * current) and caches it; make that first call before any stream capture.  All calls on a device share the one
+ * array: calls that overlap on the GPU (other streams, other threads) race and must be serialised by the caller. */
+int xcb_moe_forward_static(const XcbMoeWeights* weights, const XcbMoeArgs* args, cudaStream_t stream);
+
 /* Synchronise `stream`, read the workspace status bits into *device_status, clear them.
  * Returns XCB_OK if none were set, XCB_ERR_DEVICE otherwise. */
 int xcb_moe_read_status(void* workspace, int32_t* device_status, cudaStream_t stream);

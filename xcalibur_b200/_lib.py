@@ -24,6 +24,7 @@ XCB_STATUS_BAD_EXPERT = 2
 XCB_STATUS_NAN_SCALE = 4
 XCB_STATUS_CAPACITY = 8
 XCB_FLAG_POST_NORM = 1
+XCB_STATIC_SCRATCH_BYTES = 8 << 20
 
 # every symbol include/xcb_moe.h declares
 EXPORTS = (
@@ -37,6 +38,7 @@ EXPORTS = (
     "xcb_moe_forward",
     "xcb_moe_route",
     "xcb_moe_experts",
+    "xcb_moe_forward_static",
     "xcb_moe_read_status",
     "xcb_nvfp4_quantize",
 )
@@ -83,6 +85,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "xcb_moe_forward": (ctypes.c_int, [ctypes.POINTER(XcbMoeWeights), ctypes.POINTER(XcbMoeArgs), P, SZ, P]),
         "xcb_moe_route": (ctypes.c_int, [ctypes.POINTER(XcbMoeWeights), ctypes.POINTER(XcbMoeArgs), P, SZ, P]),
         "xcb_moe_experts": (ctypes.c_int, [ctypes.POINTER(XcbMoeWeights), ctypes.POINTER(XcbMoeArgs), P, SZ, P]),
+        "xcb_moe_forward_static": (ctypes.c_int, [ctypes.POINTER(XcbMoeWeights), ctypes.POINTER(XcbMoeArgs), P]),
         "xcb_moe_read_status": (ctypes.c_int, [P, ctypes.POINTER(I32), P]),
         "xcb_nvfp4_quantize": (ctypes.c_int, [P, I32, I32, I32, P, P, P, P, P]),
     }

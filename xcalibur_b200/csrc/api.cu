@@ -1,6 +1,8 @@
 // extern "C" boundary (include/xcb_moe.h): argument validation, workspace carving, launch sequencing.
 #include <string.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "workspace.cuh"
 
@@ -182,6 +184,49 @@ int xcb_moe_forward(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_
   rc = launch_route(rp, stream);
   if (rc != XCB_OK) return rc;
   return launch_skinny(sp, stream);
+}
+
+// ------------------------------------------------------------------------------------------------ allocation-free
+// Scratch for xcb_moe_forward_static: a file-scope device array, so callers that may not allocate device memory
+// still get a workspace.  Every GPU that loads this library reserves it until the process exits.
+static __device__ __align__(256) unsigned char g_static_scratch[XCB_STATIC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_static_mu;
+constexpr int kMaxDevices = 128;
+void* g_static_ptr[kMaxDevices] = {};
+
+// Device address of g_static_scratch on the current device.  In host code the array's name is only a host-side
+// stand-in, so the address is looked up once per device (with that device current) and cached.
+int static_scratch_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return XCB_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p) return XCB_ERR_CUDA;
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return XCB_OK;
+}
+}  // namespace
+
+int xcb_moe_forward_static(const XcbMoeWeights* w, const XcbMoeArgs* a, cudaStream_t stream) {
+  if (!w || !a) return XCB_ERR_INVALID_ARG;
+  int rc = shape_ok(&w->shape);
+  if (rc != XCB_OK) return rc;
+  if (a->tokens < 0 || a->top_k <= 0) return XCB_ERR_INVALID_ARG;
+  if (a->tokens == 0) return XCB_OK;
+  const WsLayout L = ws_layout(w->shape.num_experts, w->shape.hidden, w->shape.inter, a->tokens, a->top_k);
+  if (L.total > (size_t)XCB_STATIC_SCRATCH_BYTES) return XCB_ERR_WORKSPACE;  // call too large for the fixed scratch
+  void* ws = nullptr;
+  rc = static_scratch_address(&ws);
+  if (rc != XCB_OK) return rc;
+  // The array keeps the previous call's contents: clear the control words (status bits and counters) that the
+  // kernels expect to start at zero; every other region is rewritten by the call before it is read.
+  if (cudaMemsetAsync(ws, 0, kCtlWords * sizeof(int), stream) != cudaSuccess) return XCB_ERR_CUDA;
+  return xcb_moe_forward(w, a, ws, (size_t)XCB_STATIC_SCRATCH_BYTES, stream);
 }
 
 int xcb_moe_read_status(void* ws, int32_t* device_status, cudaStream_t stream) {
