@@ -145,6 +145,16 @@ int xcb_moe_forward_static(const XcbMoeWeights* weights, const XcbMoeArgs* args,
  * Returns XCB_OK if none were set, XCB_ERR_DEVICE otherwise. */
 int xcb_moe_read_status(void* workspace, int32_t* device_status, cudaStream_t stream);
 
+/* HBM read-bandwidth probe (diagnostic; replaces the reference's bulk-copy probes, moe_w4a16.py:2890-3061):
+ * streams `bytes` from `src` (1 KB aligned) with mode 0 = 1-D bulk-copy ring (stages x chunk bytes per CTA, chunk a
+ * multiple of 1 KB),
+ * 1 = the same with an L2 evict-first hint, 2 = 16-byte vector loads; ctas_per_sm CTAs of `threads` threads per SM.
+ * With `regions` (device int64 byte offsets, `nreg` of them) the CTAs split into nreg groups that each stream one
+ * region of bytes/nreg bytes, as the decode kernel streams a few experts.  Time it with events on `stream`;
+ * status gets XCB_STATUS_DEVICE_TIMEOUT if a ring wait expired. */
+int xcb_hbm_probe(const void* src, size_t bytes, int mode, int chunk, int stages, int ctas_per_sm, int threads,
+                  const long long* regions, int nreg, int32_t* status, float* sink, cudaStream_t stream);
+
 /* Quantise fp32 weights [E, R, K] to NVFP4 (gs = amax/(6*448) per expert, sf = e4m3(block_amax/6/gs),
  * codes RNE to E2M1): codes [E, R, K/2], sf [E, R, K/16], gs [E].  A utility for synthetic weights; the
  * reference receives already-quantised weights.  amax_scratch: device float [E] (zeroed by this call). */

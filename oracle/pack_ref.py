@@ -58,6 +58,31 @@ def _apply_T(words: np.ndarray) -> np.ndarray:
     return (tabs[0][w & 255] ^ tabs[1][(w >> 8) & 255] ^ tabs[2][(w >> 16) & 255] ^ tabs[3][w >> 24]).astype(np.uint32)
 
 
+def join_units(code_bytes: np.ndarray, scale_bytes: np.ndarray) -> np.ndarray:
+    """[nb, nS*512] codes + [nb, nS*64] scales -> [nb, 9K] units: per group of 16 slices, its codes then its scales."""
+    nb = code_bytes.shape[0]
+    nS = code_bytes.shape[1] // 512
+    parts = []
+    for g0 in range(0, nS, 16):
+        ns = min(16, nS - g0)
+        parts.append(code_bytes[:, g0 * 512:(g0 + ns) * 512])
+        parts.append(scale_bytes[:, g0 * 64:(g0 + ns) * 64])
+    return np.concatenate(parts, axis=1).reshape(nb, -1)
+
+
+def split_units(units: np.ndarray, K: int):
+    """Inverse of join_units: [nb, 9K] -> ([nb, nS*512] codes, [nb, nS*64] scales)."""
+    nS = K // 64
+    cs, ss = [], []
+    off = 0
+    for g0 in range(0, nS, 16):
+        ns = min(16, nS - g0)
+        cs.append(units[:, off:off + ns * 512])
+        ss.append(units[:, off + ns * 512:off + ns * 576])
+        off += ns * 576
+    return np.concatenate(cs, axis=1), np.concatenate(ss, axis=1)
+
+
 def pack_matrix(codes: np.ndarray, sf: np.ndarray, gate_up: bool) -> np.ndarray:
     """One expert matrix (codes [R, K/2], sf [R, K/16]) -> packed bytes [R/16 units, 9K]."""
     R, K2 = codes.shape
@@ -88,7 +113,7 @@ def pack_matrix(codes: np.ndarray, sf: np.ndarray, gate_up: bool) -> np.ndarray:
     blk = 4 * (4 * S4 + s4) + tt                                 # scale block of (slice, t)
     scl = sb[:, h, g, blk]                                        # [rb, S4, g, t, s4, h]
     scale_bytes = np.ascontiguousarray(scl).reshape(nb, K)
-    return np.concatenate([code_bytes, scale_bytes], axis=1)
+    return join_units(code_bytes, scale_bytes)
 
 
 def pack_tensor(codes: np.ndarray, sf: np.ndarray, gate_up: bool) -> np.ndarray:
@@ -100,14 +125,15 @@ def unpack_matrix_values(units: np.ndarray, R: int, K: int, gate_up: bool) -> np
     """Decode packed units back to fp32 weights (without gs) in the ORIGINAL row order, the kernel's way:
     run D on every word, read each bf16 field (value e2m1 * 2^-126), multiply by the scale code's value."""
     nb, nS = R // 16, K // 64
-    words = units[:, : nS * 512].copy().view(np.uint32).reshape(nb, nS, 8, 4, 4)    # rb, S, g, t, j
+    code_bytes, scale_bytes = split_units(units, K)
+    words = np.ascontiguousarray(code_bytes).view(np.uint32).reshape(nb, nS, 8, 4, 4)   # rb, S, g, t, j
     M = packer.FIELD_MASK
     q = words.astype(np.uint64)
     rotl = lambda v, s: ((v << s) | (v >> (32 - s))) & 0xFFFFFFFF
     u6 = (q << 6) & 0xFFFFFFFF
     regs = [q & M, (q << 4) & M, (u6 ^ rotl(q, 10)) & M, (u6 ^ rotl(q, 12)) & M]
     out = np.zeros((nb, 16, K), dtype=np.float32)
-    sb = units[:, nS * 512:].reshape(nb, nS // 4, 8, 4, 4, 2)                        # rb, S4, g, t, s4, h
+    sb = np.ascontiguousarray(scale_bytes).reshape(nb, nS // 4, 8, 4, 4, 2)          # rb, S4, g, t, s4, h
     for i, r in enumerate(regs):
         for hh in range(2):
             bits = ((r >> (16 * hh)) & 0xFFFF).astype(np.uint32) << 16

@@ -270,3 +270,39 @@ def test_batch_invariance_at_prefill_size(dev):
     assert torch.isfinite(out.float()).all()
     got = out.index_select(0, rows)
     assert torch.allclose(got.float(), small.float(), rtol=1e-2, atol=1e-2)
+
+
+def test_no_local_route_gives_zero_output(dev):
+    """Every route outside the held experts: the single-launch path still writes a zero output."""
+    from xcalibur_b200 import kernel_fn, prepare
+
+    rng = np.random.default_rng(51)
+    E, H, I, T, k = 8, 256, 256, 3, 2
+    w = _weights_from_np(moe_ref.make_weights(rng, E, H, I), dev)
+    state = prepare(w, local_start=0, local_count=4, n_experts=E)
+    x = torch.randn((T, H), device=dev).to(torch.bfloat16)
+    ids = torch.tensor([[4, 5], [6, 7], [7, 4]], dtype=torch.int64, device=dev)
+    data = {"hidden_states": x, "topk_ids": ids, "topk_weights": torch.full((T, k), 0.5, device=dev),
+            "config": {"bs": T, "d_hidden": H, "d_expert": I, "n_experts": E, "local_start": 0, "local_count": 4,
+                       "top_k": k, "sharding": "ep2"}}
+    out = kernel_fn(data, state)
+    torch.cuda.synchronize()
+    assert not out.float().abs().sum().item()
+
+
+def test_repeated_expert_within_a_token(dev):
+    """Precomputed routing may name one expert twice for a token (T=1): both routes count."""
+    from xcalibur_b200 import PreparedMoE
+
+    rng = np.random.default_rng(52)
+    E, H, I, k = 4, 512, 256, 4
+    w = moe_ref.make_weights(rng, E, H, I)
+    weights = _weights_from_np(w, dev)
+    layer = PreparedMoE(*weights.values())
+    x, _ = moe_ref.make_inputs(rng, 1, H, E)
+    xd = torch.from_numpy(x.view(np.int16)).to(dev).view(torch.bfloat16)
+    ids = np.array([[2, 2, 0, 2]], np.int32)
+    wts = np.array([[0.4, 0.3, 0.2, 0.1]], np.float32)
+    out = layer.forward(xd, None, topk_ids=torch.from_numpy(ids).to(dev), topk_weights=torch.from_numpy(wts).to(dev))
+    torch.cuda.synchronize()
+    assert_close_bf16(out, oracle_layer(xd, weights, ids, wts))

@@ -41,6 +41,7 @@ EXPORTS = (
     "xcb_moe_forward_static",
     "xcb_moe_read_status",
     "xcb_nvfp4_quantize",
+    "xcb_hbm_probe",
 )
 
 
@@ -88,6 +89,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "xcb_moe_forward_static": (ctypes.c_int, [ctypes.POINTER(XcbMoeWeights), ctypes.POINTER(XcbMoeArgs), P]),
         "xcb_moe_read_status": (ctypes.c_int, [P, ctypes.POINTER(I32), P]),
         "xcb_nvfp4_quantize": (ctypes.c_int, [P, I32, I32, I32, P, P, P, P, P]),
+        "xcb_hbm_probe": (ctypes.c_int, [P, SZ, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                         P, ctypes.c_int, P, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

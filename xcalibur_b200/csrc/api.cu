@@ -134,6 +134,9 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   rp->ids_out = a->topk_ids_out;
   rp->wts_out = a->topk_weights_out;
 
+  const bool small = (size_t)a->tokens * a->top_k <= (size_t)kSmallRoutes && a->tokens <= kSmallTokens;
+  int* ctl = rp->ctl;
+  *sp = SkinnyParams{};
   sp->wA = (const uint8_t*)w->gate_up;
   sp->wB = (const uint8_t*)w->down;
   sp->gsA = w->gate_up_gs;
@@ -144,17 +147,39 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   sp->wts = rp->wts;
   sp->pos = rp->pos;
   sp->jobs = rp->jobs;
-  sp->ctl = rp->ctl;
-  sp->doneA = rp->doneA;
+  sp->small_route = small ? 1 : 0;
+  sp->logits = a->router_logits;
+  sp->ids_in = a->topk_ids;
+  sp->wts_in = a->topk_weights;
+  sp->E_tot = s->total_experts;
+  sp->lo = s->expert_offset;
+  sp->E_loc = s->num_experts;
+  sp->g_ids = rp->ids;
+  sp->g_wts = rp->wts;
+  sp->g_pos = rp->pos;
+  sp->g_order = rp->order;
+  sp->g_counts = rp->counts;
+  sp->g_offsets = rp->offsets;
+  sp->ids_out = a->topk_ids_out;
+  sp->wts_out = a->topk_weights_out;
+  sp->ctl = ctl;
+  sp->doneA = small ? ctl + kCtlDoneA : rp->doneA;
+  sp->rbcnt = ctl + kCtlRowBlock;
   sp->inter = (uint16_t*)(b + L.inter);
   sp->y = (float*)(b + L.y);
-  sp->ss = rp->ss;
+  sp->ss = small ? (float*)(ctl + kCtlSS) : rp->ss;
   sp->out = a->out;
   sp->T = a->tokens;
   sp->k = a->top_k;
   sp->H = s->hidden;
   sp->I = s->inter;
+  {
+    // with precomputed ids one expert may repeat within a token, so a job can hold up to T*k tokens
+    const long long per_job = have_logits ? a->tokens : (long long)a->tokens * a->top_k;
+    sp->job_tokens = (int)(per_job < kJobTokens ? per_job : kJobTokens);
+  }
   sp->post_norm = post_norm ? 1 : 0;
+  sp->grid_combine = (post_norm || !small) ? 1 : 0;
   sp->timeout_ns = kTimeoutNs;
   return XCB_OK;
 }
@@ -165,6 +190,7 @@ int xcb_moe_route(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t 
   SkinnyParams sp;
   int rc = prepare_call(w, a, ws, ws_bytes, &rp, &sp);
   if (rc != XCB_OK || a->tokens == 0) return rc;
+  if (sp.small_route) return XCB_OK;  // small batches are routed inside the experts kernel
   return launch_route(rp, stream);
 }
 
@@ -181,8 +207,10 @@ int xcb_moe_forward(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_
   SkinnyParams sp;
   int rc = prepare_call(w, a, ws, ws_bytes, &rp, &sp);
   if (rc != XCB_OK || a->tokens == 0) return rc;
-  rc = launch_route(rp, stream);
-  if (rc != XCB_OK) return rc;
+  if (!sp.small_route) {
+    rc = launch_route(rp, stream);
+    if (rc != XCB_OK) return rc;
+  }
   return launch_skinny(sp, stream);
 }
 

@@ -93,6 +93,10 @@ __device__ __forceinline__ void bulk_g2s_stream(void* dst, const void* src, uint
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// Fire-and-forget bulk prefetch of [src, src + bytes) into L2 (16-byte aligned, size % 16 == 0).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -148,5 +152,76 @@ __device__ __forceinline__ uint16_t f2bf(float v) {
   return *reinterpret_cast<uint16_t*>(&b);
 }
 __device__ __forceinline__ float bf2f(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
+
+// Exclusive scan of n <= 1024 ints in shared memory by one warp (each lane owns a contiguous run); every lane
+// returns the total.
+__device__ __forceinline__ int warp_exclusive_scan(int* a, int n) {
+  const int lane = threadIdx.x & 31;
+  const int per = (n + 31) / 32;
+  const int b = min(n, lane * per), e = min(n, b + per);
+  int s = 0;
+  for (int i = b; i < e; ++i) s += a[i];
+  int incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  int run = incl - s;
+  for (int i = b; i < e; ++i) {
+    const int v = a[i];
+    a[i] = run;
+    run += v;
+  }
+  return __shfl_sync(0xffffffffu, incl, 31);
+}
+
+// Order-preserving map float -> uint32 (larger float, larger key; -0 and +0 share a key, so they tie).
+__device__ __forceinline__ uint32_t float_key(float f) {
+  const uint32_t b = __float_as_uint(f == 0.f ? 0.f : f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+// Top-k of one token's logits by one warp: rank by value descending, ties to the lower index; weights = softmax
+// over the selected logits (summed in route order).  Lane s < k returns route s in (id, w).  E <= 512.
+// Each round is two warp reductions: the largest key, then the lowest index holding it.
+__device__ __forceinline__ void warp_topk(const float* row, int E, int k, int& id, float& w) {
+  const int lane = threadIdx.x & 31;
+  const int per = (E + 31) / 32;
+  uint32_t key[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int e = lane + 32 * j;
+    key[j] = (j < per && e < E) ? float_key(row[e]) : 0u;  // 0 is below every real key
+  }
+  uint32_t used = 0, my_key = 0;
+  int my_i = -1;
+  for (int s = 0; s < k; ++s) {
+    uint32_t bk = 0;
+    int bj = -1;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (!((used >> j) & 1u) && key[j] > bk) {  // strict: the lower j (lower index) wins a tie
+        bk = key[j];
+        bj = j;
+      }
+    const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+    const uint32_t mi = __reduce_min_sync(0xffffffffu, (bj >= 0 && bk == mk) ? (uint32_t)(lane + 32 * bj) : 0xffffffffu);
+    if ((int)(mi & 31) == lane) used |= 1u << (mi >> 5);
+    if (lane == s) {
+      my_key = mk;
+      my_i = (int)mi;
+    }
+  }
+  const float top = key_float(__shfl_sync(0xffffffffu, my_key, 0));
+  const float ex = (lane < k) ? expf(key_float(my_key) - top) : 0.f;
+  float den = 0.f;
+  for (int s = 0; s < k; ++s) den += __shfl_sync(0xffffffffu, ex, s);
+  id = my_i;
+  w = ex / den;
+}
 
 }  // namespace xcb

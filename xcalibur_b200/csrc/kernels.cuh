@@ -32,18 +32,36 @@ struct SkinnyParams {
   const float* gsB;
   const uint16_t* normw;  // bf16 [H] or null
   const uint16_t* x;      // bf16 [T, H]
+  // routing produced by route_kernel (small_route == 0)
   const int* order;       // permuted position -> flat route
   const float* wts;       // flat route weights
   const int* pos;         // flat route -> permuted position (-1: not local)
   const int4* jobs;       // (expert, p0, ntok, 0)
+  // in-kernel routing (small_route == 1): inputs, and where CTA 0 publishes the tables
+  int small_route;
+  const float* logits;
+  const int* ids_in;
+  const float* wts_in;
+  int E_tot, lo, E_loc;
+  int* g_ids;
+  float* g_wts;
+  int* g_pos;
+  int* g_order;
+  int* g_counts;
+  int* g_offsets;
+  int* ids_out;
+  float* wts_out;
   int* ctl;
-  int* doneA;
+  int* doneA;             // per-job phase-A counters
+  int* rbcnt;             // per-16-row-block phase-B counters
   uint16_t* inter;        // bf16 [routes, I]
   float* y;               // fp32 [routes, H]
   float* ss;              // fp32 [routes]
   uint16_t* out;          // bf16 [T, H]
   int T, k, H, I;
+  int job_tokens;         // most tokens one job can hold (sizes the activation staging)
   int post_norm;
+  int grid_combine;       // 1: grid barrier + distributed combine; 0: per-row-block combine by the last unit
   unsigned long long timeout_ns;
 };
 

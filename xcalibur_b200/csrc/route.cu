@@ -17,35 +17,6 @@
 namespace xcb {
 
 constexpr int kRouteThreads = 1024;
-constexpr int kRouteMaxE = 512;      // router width (16 logits per lane)
-
-__device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
-  return va > vb || (va == vb && ia < ib);
-}
-
-// Exclusive scan of n <= 1024 ints in shared memory by warp 0 (each lane owns a contiguous run).  Returns the total.
-__device__ int warp0_exclusive_scan(int* a, int n, int* total_out) {
-  const int lane = threadIdx.x & 31;
-  const int per = (n + 31) / 32;
-  const int b = lane * per, e = min(n, b + per);
-  int s = 0;
-  for (int i = b; i < e; ++i) s += a[i];
-  int incl = s;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    int v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
-  }
-  int run = incl - s;
-  for (int i = b; i < e; ++i) {
-    int v = a[i];
-    a[i] = run;
-    run += v;
-  }
-  const int total = __shfl_sync(0xffffffffu, incl, 31);
-  if (lane == 0) *total_out = total;
-  return total;
-}
 
 __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(RouteParams p) {
   extern __shared__ int route_smem[];
@@ -62,53 +33,12 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(RouteParams p) 
 
   // ---- 1. routes and histogram
   if (p.logits) {
-    const int per = (p.E_tot + 31) / 32;
     for (int t = warp; t < p.T; t += kRouteThreads / 32) {
-      float v[kRouteMaxE / 32];
-      const float* row = p.logits + (size_t)t * p.E_tot;
-#pragma unroll
-      for (int j = 0; j < kRouteMaxE / 32; ++j) {
-        const int e = lane + 32 * j;
-        v[j] = (j < per && e < p.E_tot) ? row[e] : -INFINITY;
-      }
-      uint32_t used = 0;
-      float sel_v = 0.f;
-      float my_v = 0.f;
-      int my_i = -1;
-      for (int s = 0; s < p.k; ++s) {
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int j = 0; j < kRouteMaxE / 32; ++j) {
-          const int e = lane + 32 * j;
-          if (j < per && e < p.E_tot && !((used >> j) & 1u) && better(v[j], e, bv, bi)) {
-            bv = v[j];
-            bi = e;
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-          if (better(ov, oi, bv, bi)) {
-            bv = ov;
-            bi = oi;
-          }
-        }
-        if ((bi & 31) == lane) used |= 1u << (bi >> 5);
-        if (s == 0) sel_v = bv;
-        if (lane == s) {
-          my_v = bv;
-          my_i = bi;
-        }
-      }
-      // softmax over the selected logits: numerators on lanes 0..k-1, denominator summed in route order
-      const float ex = (lane < p.k) ? expf(my_v - sel_v) : 0.f;
-      float den = 0.f;
-      for (int s = 0; s < p.k; ++s) den += __shfl_sync(0xffffffffu, ex, s);
+      int my_i;
+      float w;
+      warp_topk(p.logits + (size_t)t * p.E_tot, p.E_tot, p.k, my_i, w);
       if (lane < p.k) {
         const int f = t * p.k + lane;
-        const float w = ex / den;
         p.ids[f] = my_i;
         p.wts[f] = w;
         if (p.ids_out) p.ids_out[f] = my_i;
@@ -141,8 +71,14 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(RouteParams p) 
     jcnt[e] = (cnt[e] + kJobTokens - 1) / kJobTokens;
   }
   __syncthreads();
-  if (warp == 0) warp0_exclusive_scan(base, p.E_loc, &tot_routes);
-  if (warp == 1) warp0_exclusive_scan(jcnt, p.E_loc, &tot_jobs);
+  if (warp == 0) {
+    const int tot = warp_exclusive_scan(base, p.E_loc);
+    if (lane == 0) tot_routes = tot;
+  }
+  if (warp == 1) {
+    const int tot = warp_exclusive_scan(jcnt, p.E_loc);
+    if (lane == 0) tot_jobs = tot;
+  }
   __syncthreads();
   for (int e = tid; e < p.E_loc; e += kRouteThreads) {
     p.counts[e] = cnt[e];

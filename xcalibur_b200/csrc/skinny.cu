@@ -1,211 +1,496 @@
-// Decode-path MoE kernel: one persistent launch runs gate_up + SwiGLU (phase A), down (phase B) and the
-// weighted combine for jobs of at most 8 tokens.  This is the HBM-bound path (T = 1 decode streams ~200 MB of
-// FP4 weights for 8 experts), so it is built around the weight stream:
+// Decode-path MoE kernel: one persistent launch runs (for small batches) the router, gate_up + SwiGLU (phase A),
+// down (phase B) and the weighted combine, for jobs of at most 8 tokens.  This is the HBM-bound path (T = 1
+// decode streams ~200 MB of FP4 weights for 8 experts), so the kernel is one continuous weight stream per SM:
 //
-// * One CTA per SM (1 x 288 threads): warp 8 is a producer that streams packed units through an 8-stage
-//   shared-memory ring with 1-D bulk copies (TMA engine, L2 evict-first), 9 KB per stage (16 slices of 64 k).
-// * Warps 0..7 split each unit's k slices; per 4 packed words a lane runs the GF(2) decoder (8 integer ops per
-//   8 weights), one bf16x2 multiply per register by the block scale pair, and one m16n8k16 tensor-core step
-//   whose A operand comes straight from registers.  A register-fed MMA reads no shared memory for the weights,
-//   which is why this path does not use tcgen05: at T <= 8 the weights are used once, and staging decoded bf16
-//   tiles through shared memory for tcgen05 would double the shared-memory traffic per weight.
-// * Work: CTA c owns a contiguous range of phase-A units (job, 16-row block) and of phase-B units.  A phase-B
-//   unit waits (bounded spin) until all phase-A units of its job are done; meanwhile the producer keeps
-//   streaming phase-B weights, so HBM stays busy across the phase boundary.
-// * After a grid barrier (bounded) every CTA combines (token, 1024-column) items:
-//   out = bf16(sum_s w_s * y_s) or the post-norm form.  The last CTA to exit zeroes the grid counters; the
-//   per-job counters are zeroed by the router launch that precedes every call.
+// * 19 warps per CTA, one CTA per SM, each warp one role:
+//   - warp 16 streams packed weights through a shared-memory ring (18 KB stages, one 1-D bulk copy on the TMA
+//     engine each, L2 evict-first); 18 KB copies are what a single issuing thread needs to reach HBM rate;
+//   - warp 17 stages each segment's activation rows (x for phase A, the job's SwiGLU output for phase B, after an
+//     acquire on that job's phase-A counter) into double-buffered shared memory, also with bulk copies;
+//   - warp 18 publishes finished work: one GPU-scope fence and one counter update per segment (phase A: the
+//     job's unit credits; phase B: the 16-row blocks' counts, combining a block when it completes);
+//   - warps 0..15 only compute: slice w of every 16-slice group, the GF(2) decoder (8 integer ops per 8
+//     weights), one bf16x2 multiply per register by the block-scale pair and an m16n8k16 tensor-core step fed
+//     from registers.  At T <= 8 tokens per expert the weights are used once, and staging decoded bf16 tiles
+//     through shared memory for tcgen05 would add 4 B of shared-memory traffic per weight.
+// * Units (16 output rows x full K) are reduced without a barrier: each warp drops its partial sums into a slot,
+//   the last to arrive sums the 16 partials in warp order (deterministic) and writes the epilogue.
+// * Wave schedule for few jobs: every CTA takes an equal share of every job, in the order A0 A1 B0 A2 B1 ...,
+//   so phase B of a job starts about one job after its phase A and the weight stream never waits for it.  With
+//   many jobs each CTA takes contiguous unit ranges instead.
+// * Combine: the CTA whose phase-B units complete a 16-row block forms out = bf16(sum_s w_s * y_s) for it; with the
+//   post-norm, or for large batches, a bounded grid barrier precedes a combine spread over all CTAs.
+// * Small batches (T*k <= 256) route inside the kernel (every CTA computes the same tables), so a decode step is
+//   a single launch.  Every wait is bounded by %globaltimer; on timeout a status bit is set and the kernel drains.
 //
-// Reference counterpart: moe_fused's skinny path (kernels/moe_w4a16_h200/moe_w4a16.py:754-1133 skinny ring,
-// :1602-1785 warp-specialised epilogues, :2617-2641 grid barrier, :2654-2796 final combine).
+// Reference counterpart: moe_fused's skinny path (kernels/moe_w4a16_h200/moe_w4a16.py:491-611 route,
+// :754-1133 skinny ring, :1602-1785 warp-specialised epilogues, :2617-2641 grid barrier, :2654-2796 final sum).
 #include "common.cuh"
 #include "kernels.cuh"
 #include "workspace.cuh"
 
 namespace xcb {
 
-constexpr int SK_NW = 8;
-constexpr int SK_THREADS = (SK_NW + 1) * 32;
-constexpr int SK_CS = 16;                               // slices (64 k) per stage
-constexpr int SK_CODE_BYTES = SK_CS * 512;              // 8 KB codes
-constexpr int SK_STAGE_BYTES = SK_CODE_BYTES + SK_CS * 64;  // + 1 KB scale codes
-constexpr int SK_NSTAGE = 8;
+// Optional timeline trace (builds with -DXCB_TRACE=1 only): %globaltimer stamps and wait counters per CTA, read back
+// with xcb_trace_read.  Off in the shipped library.
+#ifndef XCB_TRACE
+#define XCB_TRACE 0
+#endif
+#if XCB_TRACE
+constexpr int kTraceSlots = 32;
+__device__ unsigned long long g_trace[1024 * kTraceSlots];
+#define TRACE_AT(slot) (g_trace[blockIdx.x * kTraceSlots + (slot)] = gtimer())
+#define TRACE_ADD(slot, v) atomicAdd(&g_trace[blockIdx.x * kTraceSlots + (slot)], (unsigned long long)(v))
+#else
+#define TRACE_AT(slot) ((void)0)
+#define TRACE_ADD(slot, v) ((void)0)
+#endif
 
-struct SkSmemOffsets {
-  int ring, xs, red, bars, total, pitch_max;
+constexpr int SK_NW = 16;                               // compute warps
+constexpr int SK_W_PROD = SK_NW;                        // weight producer warp
+constexpr int SK_W_ACT = SK_NW + 1;                     // activation staging warp
+constexpr int SK_W_SIG = SK_NW + 2;                     // signalling warp
+constexpr int SK_W_EPI = SK_NW + 3;                     // reduction + epilogue warp
+constexpr int SK_THREADS = (SK_NW + 4) * 32;
+constexpr int SK_GS = 16;                               // slices (64 k) per group = one per compute warp
+constexpr int SK_GROUP_BYTES = SK_GS * 576;             // 8 KB codes + 1 KB scale codes
+constexpr int SK_STAGE_BYTES = 2 * SK_GROUP_BYTES;      // a stage is two groups: one 18 KB bulk copy
+constexpr int SK_MAX_STAGES = 16;
+constexpr int SK_MAX_SLOTS = 4;                         // reduction slots
+constexpr int SK_SLOT_FLOATS = SK_NW * 32 * 4;
+constexpr int SK_MAX_BUFS = 2;                          // activation buffers
+constexpr int SK_SEG_RING = 64;                         // per-segment completion counters
+constexpr int SK_WAVE_JOBS = 0;                         // at most this many jobs: wave schedule (measured slower:
+                                                        // per-job staging and dependency stalls; kept switchable)
+constexpr long long SK_L2_PREFETCH_BYTES = 96ll << 20;  // phase-B weights up to this size are prefetched into L2
+constexpr int SK_SMEM_LIMIT = 227 * 1024;
+
+// Shared-memory routing tables of the in-kernel router.
+struct SkRoute {
+  int ids[kSmallRoutes];
+  float wts[kSmallRoutes];
+  int pos[kSmallRoutes];
+  int order[kSmallRoutes];
+  int4 jobs[kSmallRoutes];
+  int counts[512];
+  int offsets[513];
+  int jcnt[512];
+  int njobs, nroutes;
 };
 
-__host__ __device__ inline SkSmemOffsets sk_smem(int H, int I) {
-  SkSmemOffsets o;
-  const int kmax = H > I ? H : I;
-  o.pitch_max = kmax * 2 + 16;
-  o.ring = 0;
-  o.xs = SK_NSTAGE * SK_STAGE_BYTES;
-  o.red = o.xs + 8 * o.pitch_max;
-  o.bars = o.red + 2 * SK_NW * 32 * 4 * 4;
-  o.total = o.bars + 2 * SK_NSTAGE * 8 + 16;
+// Control block: mbarriers, reduction-slot and segment bookkeeping.
+struct SkCtl {
+  uint64_t full[SK_MAX_STAGES], empty[SK_MAX_STAGES];
+  uint64_t act_full[SK_MAX_BUFS], act_empty[SK_MAX_BUFS];
+  uint64_t slot_full[SK_MAX_SLOTS];  // 16 compute warps deposited their partial sums of a unit
+  uint64_t slot_free[SK_MAX_SLOTS];  // the epilogue warp has consumed the slot
+  int seg_cnt[SK_SEG_RING];
+  int seg_gen[SK_SEG_RING];
+  float gs[2][kSmallRoutes];  // phase A / B global scale (x 2^52) of each job (jobs < kSmallRoutes; else global)
+  int list[1024];             // scratch: row blocks a segment completed
+  int nlist;
+};
+
+struct SkLayout {
+  int buf, red, route, ctl, ring, total, nstage, nbuf, nslot, rows, pitch;
+};
+
+__host__ __device__ inline SkLayout sk_layout(int H, int I, int job_tokens, int small_route) {
+  SkLayout o;
+  o.pitch = (H > I ? H : I) * 2 + 16;
+  o.rows = job_tokens < kJobTokens ? job_tokens : kJobTokens;
+  if (o.rows < 1) o.rows = 1;
+  const int route = small_route ? (int)sizeof(SkRoute) : 0;
+  o.nstage = 0;
+  for (int nbuf = SK_MAX_BUFS; nbuf >= 1; --nbuf) {
+    for (int nslot = SK_MAX_SLOTS; nslot >= 2; nslot /= 2) {
+      o.nbuf = nbuf;
+      o.nslot = nslot;
+      o.buf = 0;
+      o.red = o.buf + nbuf * o.rows * o.pitch;
+      o.route = o.red + nslot * SK_SLOT_FLOATS * 4;
+      o.ctl = (o.route + route + 15) & ~15;
+      o.ring = (o.ctl + (int)sizeof(SkCtl) + 1023) & ~1023;
+      const int ns = (SK_SMEM_LIMIT - o.ring) / SK_STAGE_BYTES;
+      o.nstage = ns > SK_MAX_STAGES ? SK_MAX_STAGES : ns;
+      o.total = o.ring + o.nstage * SK_STAGE_BYTES;
+      if (o.nstage >= 6) return o;
+    }
+  }
   return o;
 }
 
-// One 64-k slice for one warp: 4 packed words -> 4 tensor-core steps.
-__device__ __forceinline__ void sk_slice(const uint8_t* stage, int s, const uint8_t* xrow, int S, int lane, int t,
-                                         float* acc) {
-  const uint4 cw = *reinterpret_cast<const uint4*>(stage + s * 512 + lane * 16);
-  const uint32_t sc = *reinterpret_cast<const uint16_t*>(stage + SK_CODE_BYTES + (s >> 2) * 256 + lane * 8 + (s & 3) * 2);
+// The units of one CTA, cut into segments of one job and one phase, in processing order.
+struct SkSegments {
+  int wave, njobs, nrbA, nrbB, G, bid;
+  long long a0, a1, b0, b1;  // contiguous mode: this CTA's unit ranges
+  int jA0, nAj, jB0, nBj;    // contiguous mode: jobs the ranges touch
+
+  __device__ void init(int nj, int nA_rb, int nB_rb, int grid, int b, int wave_mode) {
+    njobs = nj;
+    nrbA = nA_rb;
+    nrbB = nB_rb;
+    G = grid;
+    bid = b;
+    wave = wave_mode;
+    const long long nA = (long long)njobs * nrbA, nB = (long long)njobs * nrbB;
+    a0 = nA * bid / G;
+    a1 = nA * (bid + 1) / G;
+    b0 = nB * bid / G;
+    b1 = nB * (bid + 1) / G;
+    jA0 = (int)(a0 / nrbA);
+    nAj = a1 > a0 ? (int)((a1 - 1) / nrbA) - jA0 + 1 : 0;
+    jB0 = (int)(b0 / nrbB);
+    nBj = b1 > b0 ? (int)((b1 - 1) / nrbB) - jB0 + 1 : 0;
+  }
+  __device__ int count() const { return wave ? 2 * njobs : nAj + nBj; }
+  // Segment i (possibly empty): phase, job, unit range [u0, u1) in the phase's unit numbering (job * nrb + rb).
+  __device__ void at(int i, int& ph, int& job, long long& u0, long long& u1) const {
+    if (wave) {
+      if (i == 0) { ph = 0; job = 0; }
+      else if (i == 2 * njobs - 1) { ph = 1; job = njobs - 1; }
+      else if (i & 1) { ph = 0; job = (i + 1) / 2; }
+      else { ph = 1; job = (i + 1) / 2 - 1; }
+      const int nrb = ph ? nrbB : nrbA;
+      u0 = (long long)job * nrb + (long long)nrb * bid / G;
+      u1 = (long long)job * nrb + (long long)nrb * (bid + 1) / G;
+    } else if (i < nAj) {
+      ph = 0;
+      job = jA0 + i;
+      u0 = a0 > (long long)job * nrbA ? a0 : (long long)job * nrbA;
+      u1 = a1 < (long long)(job + 1) * nrbA ? a1 : (long long)(job + 1) * nrbA;
+    } else {
+      ph = 1;
+      job = jB0 + i - nAj;
+      u0 = b0 > (long long)job * nrbB ? b0 : (long long)job * nrbB;
+      u1 = b1 < (long long)(job + 1) * nrbB ? b1 : (long long)(job + 1) * nrbB;
+    }
+  }
+};
+
+// One 64-k slice for one warp: 4 packed words -> 4 tensor-core steps on two accumulator chains.  `grp` is the
+// group (ns slices: codes, then scale codes) in shared memory, s the slice within it, S its index in the unit.
+__device__ __forceinline__ void sk_slice(const uint8_t* grp, int ns, int s, const uint8_t* xrow, int S, int lane, int t,
+                                         float* acc0, float* acc1) {
+  const uint4 cw = *reinterpret_cast<const uint4*>(grp + s * 512 + lane * 16);
+  const uint32_t sc = *reinterpret_cast<const uint16_t*>(grp + ns * 512 + (s >> 2) * 256 + lane * 8 + (s & 3) * 2);
   const uint4 xa = *reinterpret_cast<const uint4*>(xrow + S * 128 + t * 32);
   const uint4 xb = *reinterpret_cast<const uint4*>(xrow + S * 128 + t * 32 + 16);
   const uint32_t s2 = scale_pair(sc);
-  const uint32_t qw[4] = {cw.x, cw.y, cw.z, cw.w};
-  const uint32_t xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint32_t r0, r1, r2, r3;
-    decode_fp4x8(qw[j], r0, r1, r2, r3);
-    mma_16816(acc, bf16x2_mul_lo(r0, s2), bf16x2_mul_hi(r1, s2), bf16x2_mul_lo(r2, s2), bf16x2_mul_hi(r3, s2),
-              xv[2 * j], xv[2 * j + 1]);
+  uint32_t r0, r1, r2, r3;
+  decode_fp4x8(cw.x, r0, r1, r2, r3);
+  mma_16816(acc0, bf16x2_mul_lo(r0, s2), bf16x2_mul_hi(r1, s2), bf16x2_mul_lo(r2, s2), bf16x2_mul_hi(r3, s2), xa.x, xa.y);
+  decode_fp4x8(cw.y, r0, r1, r2, r3);
+  mma_16816(acc1, bf16x2_mul_lo(r0, s2), bf16x2_mul_hi(r1, s2), bf16x2_mul_lo(r2, s2), bf16x2_mul_hi(r3, s2), xa.z, xa.w);
+  decode_fp4x8(cw.z, r0, r1, r2, r3);
+  mma_16816(acc0, bf16x2_mul_lo(r0, s2), bf16x2_mul_hi(r1, s2), bf16x2_mul_lo(r2, s2), bf16x2_mul_hi(r3, s2), xb.x, xb.y);
+  decode_fp4x8(cw.w, r0, r1, r2, r3);
+  mma_16816(acc1, bf16x2_mul_lo(r0, s2), bf16x2_mul_hi(r1, s2), bf16x2_mul_lo(r2, s2), bf16x2_mul_hi(r3, s2), xb.z, xb.w);
+}
+
+// In-kernel router for T*k <= kSmallRoutes (all warps; every CTA computes the same tables).
+__device__ void sk_route_small(const SkinnyParams& p, SkRoute& r) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
+  const int R = p.T * p.k;
+  for (int t = warp; t < p.T; t += nthr / 32) {
+    int id = -1;
+    float w = 0.f;
+    if (p.logits) {
+      warp_topk(p.logits + (size_t)t * p.E_tot, p.E_tot, p.k, id, w);
+    } else if (lane < p.k) {
+      id = p.ids_in[t * p.k + lane];
+      w = p.wts_in[t * p.k + lane];
+      if (id < 0 || id >= p.E_tot) {
+        if (blockIdx.x == 0) set_status(p.ctl + kCtlStatus, XCB_STATUS_BAD_EXPERT);
+        id = -1;
+      }
+    }
+    if (lane < p.k) {
+      r.ids[t * p.k + lane] = id;
+      r.wts[t * p.k + lane] = w;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) TRACE_AT(15);
+  // per-expert counts and each route's rank among the earlier routes of its expert (stable order)
+  for (int e = tid; e < p.E_loc; e += nthr) {
+    int c = 0;
+    for (int f = 0; f < R; ++f) c += (r.ids[f] == p.lo + e);
+    r.counts[e] = c;
+    r.offsets[e] = c;
+    r.jcnt[e] = (c + kJobTokens - 1) / kJobTokens;
+  }
+  for (int f = tid; f < R; f += nthr) {
+    const int id = r.ids[f];
+    int rank = 0;
+    for (int g = 0; g < f; ++g) rank += (r.ids[g] == id);
+    r.pos[f] = rank;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int tot = warp_exclusive_scan(r.offsets, p.E_loc);
+    if (lane == 0) {
+      r.nroutes = tot;
+      r.offsets[p.E_loc] = tot;
+    }
+  } else if (warp == 1) {
+    const int tot = warp_exclusive_scan(r.jcnt, p.E_loc);
+    if (lane == 0) r.njobs = tot;
+  }
+  __syncthreads();
+  if (tid == 0) TRACE_AT(16);
+  for (int f = tid; f < R; f += nthr) {
+    const int el = r.ids[f] - p.lo;
+    if (r.ids[f] >= 0 && el >= 0 && el < p.E_loc) {
+      const int q = r.offsets[el] + r.pos[f];
+      r.pos[f] = q;
+      r.order[q] = f;
+    } else {
+      r.pos[f] = -1;
+    }
+  }
+  for (int e = tid; e < p.E_loc; e += nthr) {
+    const int c = r.counts[e];
+    int j = r.jcnt[e];
+    for (int s0 = 0; s0 < c; s0 += kJobTokens, ++j) r.jobs[j] = make_int4(e, r.offsets[e] + s0, min(kJobTokens, c - s0), 0);
+  }
+  __syncthreads();
+  if (blockIdx.x == 0) {  // publish the routing (tests and callers read it from the workspace)
+    for (int f = tid; f < R; f += nthr) {
+      p.g_ids[f] = r.ids[f];
+      p.g_wts[f] = r.wts[f];
+      p.g_pos[f] = r.pos[f];
+      if (p.ids_out) p.ids_out[f] = r.ids[f];
+      if (p.wts_out) p.wts_out[f] = r.wts[f];
+    }
+    for (int q = tid; q < r.nroutes; q += nthr) p.g_order[q] = r.order[q];
+    for (int e = tid; e <= p.E_loc; e += nthr) {
+      if (e < p.E_loc) p.g_counts[e] = r.counts[e];
+      p.g_offsets[e] = r.offsets[e];
+    }
   }
 }
 
+
+
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  const SkSmemOffsets so = sk_smem(p.H, p.I);
-  uint8_t* ring = smem + so.ring;
-  uint8_t* xs = smem + so.xs;
-  float* red = reinterpret_cast<float*>(smem + so.red);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + so.bars);
-  uint64_t* empty = full + SK_NSTAGE;
+  const SkLayout L = sk_layout(p.H, p.I, p.job_tokens, p.small_route);
+  uint8_t* bufs = smem + L.buf;
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  SkRoute& rt = *reinterpret_cast<SkRoute*>(smem + L.route);
+  SkCtl& cb = *reinterpret_cast<SkCtl*>(smem + L.ctl);
+  uint8_t* ring = smem + L.ring;
   int* status = p.ctl + kCtlStatus;
-
+  const int NST = L.nstage, NBUF = L.nbuf, NSLOT = L.nslot;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, bid = blockIdx.x;
-  const int njobs = p.ctl[kCtlJobs];
-  const int nrbA = (2 * p.I) / 16, nrbB = p.H / 16;
-  const int nSA = p.H / 64, nSB = p.I / 64;           // slices per unit
-  const int nchA = (nSA + SK_CS - 1) / SK_CS, nchB = (nSB + SK_CS - 1) / SK_CS;
-  const long long nA = (long long)njobs * nrbA, nB = (long long)njobs * nrbB;
-  const long long a0 = nA * bid / G, a1 = nA * (bid + 1) / G;
-  const long long b0 = nB * bid / G, b1 = nB * (bid + 1) / G;
-  const size_t unitA = (size_t)9 * p.H, unitB = (size_t)9 * p.I;
 
   if (tid == 0) {
-    for (int i = 0; i < SK_NSTAGE; ++i) {
-      mbar_init(full + i, 1);
-      mbar_init(empty + i, SK_NW);
+    TRACE_AT(0);
+    for (int i = 0; i < NST; ++i) {
+      mbar_init(cb.full + i, 1);
+      mbar_init(cb.empty + i, SK_NW);
+    }
+    for (int i = 0; i < NBUF; ++i) {
+      mbar_init(cb.act_full + i, 1);
+      mbar_init(cb.act_empty + i, SK_NW);
     }
     fence_mbar_init();
   }
+  if (tid == 0) {
+    for (int i = 0; i < NSLOT; ++i) {
+      mbar_init(cb.slot_full + i, SK_NW);
+      mbar_init(cb.slot_free + i, 1);
+    }
+    fence_mbar_init();
+  }
+  for (int i = tid; i < SK_SEG_RING; i += SK_THREADS) {
+    cb.seg_cnt[i] = 0;
+    cb.seg_gen[i] = 0;
+  }
+  if (tid == 0) cb.nlist = 0;
+  if (p.small_route) sk_route_small(p, rt);
+  __syncthreads();
+  if (tid == 0) TRACE_AT(1);
+
+  const int njobs = p.small_route ? rt.njobs : p.ctl[kCtlJobs];
+  const int4* jobs = p.small_route ? rt.jobs : p.jobs;
+  const int* order = p.small_route ? rt.order : p.order;
+  const int* pos = p.small_route ? rt.pos : p.pos;
+  const float* wts = p.small_route ? rt.wts : p.wts;
+  const int nrbA = (2 * p.I) / 16, nrbB = p.H / 16;
+  const int nSA = p.H / 64, nSB = p.I / 64;  // slices per unit
+  const int nchA = ((nSA + SK_GS - 1) / SK_GS + 1) / 2, nchB = ((nSB + SK_GS - 1) / SK_GS + 1) / 2;  // stages/unit
+  const size_t unitA = (size_t)9 * p.H, unitB = (size_t)9 * p.I;
+  SkSegments segs;
+  segs.init(njobs, nrbA, nrbB, G, bid, njobs <= SK_WAVE_JOBS);
+  const int nseg = segs.count();
+  const bool gs_cached = njobs <= kSmallRoutes;
+  if (gs_cached) {
+    for (int j = tid; j < njobs; j += SK_THREADS) {
+      const int e = jobs[j].x;
+      cb.gs[0][j] = p.gsA[e] * kTwo52;
+      cb.gs[1][j] = p.gsB[e] * kTwo52;
+    }
+  }
   __syncthreads();
 
-  if (warp == SK_NW) {
-    // ------------------------------------------------------------------ producer
+  if (warp == SK_W_PROD) {
+    // ------------------------------------------------------------------ weight producer
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       int it = 0;
       bool ok = true;
-      for (int ph = 0; ph < 2 && ok; ++ph) {
-        const long long u0 = ph ? b0 : a0, u1 = ph ? b1 : a1;
+      // phase-B weights do not depend on phase A: when they fit in L2, stream them into L2 right behind this CTA's
+      // phase-A weights, so HBM sees one continuous stream and phase B reads L2 after the A -> B handoff
+      const bool prefetch_b = (long long)njobs * nrbB * (long long)unitB <= SK_L2_PREFETCH_BYTES;
+      bool prefetched = false;
+      for (int s = 0; s < nseg && ok; ++s) {
+        int ph, job;
+        long long u0, u1;
+        segs.at(s, ph, job, u0, u1);
+        if (ph == 1 && prefetch_b && !prefetched) {
+          prefetched = true;
+          for (int s2 = s; s2 < nseg; ++s2) {
+            int ph2, job2;
+            long long v0, v1;
+            segs.at(s2, ph2, job2, v0, v1);
+            if (ph2 != 1 || v1 <= v0) continue;
+            const uint8_t* first = p.wB + ((size_t)jobs[job2].x * nrbB + (size_t)(v0 - (long long)job2 * nrbB)) * unitB;
+            const size_t total = (size_t)(v1 - v0) * unitB;  // consecutive units of one job are contiguous
+            for (size_t off = 0; off < total; off += (size_t)1 << 20)
+              bulk_prefetch_l2(first + off, (uint32_t)min(total - off, (size_t)1 << 20));
+          }
+        }
         const int nrb = ph ? nrbB : nrbA, nS = ph ? nSB : nSA, nch = ph ? nchB : nchA;
         const uint8_t* wbase = ph ? p.wB : p.wA;
         const size_t ub = ph ? unitB : unitA;
-        const size_t code_bytes = (size_t)nS * 512;
+        const int e = jobs[job].x;
         for (long long u = u0; u < u1 && ok; ++u) {
-          const int jidx = (int)(u / nrb), rb = (int)(u % nrb);
-          const int e = p.jobs[jidx].x;
-          const uint8_t* unit = wbase + ((size_t)e * nrb + rb) * ub;
+          const uint8_t* unit = wbase + ((size_t)e * nrb + (size_t)(u - (long long)job * nrb)) * ub;
           for (int c = 0; c < nch; ++c, ++it) {
-            const int ns = min(SK_CS, nS - c * SK_CS);
-            const int st = it % SK_NSTAGE;
-            if (it >= SK_NSTAGE && !mbar_wait(empty + st, ((it / SK_NSTAGE) + 1) & 1, p.timeout_ns, status)) {
+            const int ns = min(2 * SK_GS, nS - c * 2 * SK_GS);
+            const int st = it % NST;
+            if (it >= NST && !mbar_wait(cb.empty + st, ((it / NST) + 1) & 1, p.timeout_ns, status)) {
               ok = false;
               break;
             }
-            uint8_t* dst = ring + st * SK_STAGE_BYTES;
-            mbar_arrive_expect_tx(full + st, ns * 576);
-            bulk_g2s_stream(dst, unit + (size_t)c * SK_CODE_BYTES, ns * 512, full + st, pol);
-            bulk_g2s_stream(dst + SK_CODE_BYTES, unit + code_bytes + (size_t)c * SK_CS * 64, ns * 64, full + st, pol);
+            mbar_arrive_expect_tx(cb.full + st, ns * 576);
+            bulk_g2s_stream(ring + st * SK_STAGE_BYTES, unit + (size_t)c * SK_STAGE_BYTES, ns * 576, cb.full + st, pol);
           }
         }
       }
-      // drain: every copy issued must have landed before this CTA may exit
-      for (int i = max(0, it - SK_NSTAGE); i < it; ++i)
-        mbar_wait(full + (i % SK_NSTAGE), (i / SK_NSTAGE) & 1, p.timeout_ns, status);
+      TRACE_AT(3);
+      for (int i = max(0, it - NST); i < it; ++i) mbar_wait(cb.full + (i % NST), (i / NST) & 1, p.timeout_ns, status);
     }
-    return;
-  }
-
-  // -------------------------------------------------------------------- consumers (warps 0..7)
-  const int g = lane >> 2, t = lane & 3;
-  int it = 0, rbuf = 0;
-  for (int ph = 0; ph < 2; ++ph) {
-    const long long u0 = ph ? b0 : a0, u1 = ph ? b1 : a1;
-    const int nrb = ph ? nrbB : nrbA, nS = ph ? nSB : nSA, nch = ph ? nchB : nchA;
-    const int K = ph ? p.I : p.H;
-    const int pitch = K * 2 + 16;
-    int cur = -1;
-    for (long long u = u0; u < u1; ++u) {
-      const int jidx = (int)(u / nrb), rb = (int)(u % nrb);
-      const int4 job = p.jobs[jidx];
-      if (jidx != cur) {
-        // stage this job's activation rows (x for phase A, inter for phase B) into shared memory
-        named_bar(1, SK_NW * 32);
-        if (ph == 1 && tid == 0) wait_geq(p.doneA + jidx, nrbA, p.timeout_ns, status);
-        named_bar(1, SK_NW * 32);
-        const int vec_per_row = K / 8;  // 16-byte vectors
-        for (int i = tid; i < 8 * vec_per_row; i += SK_NW * 32) {
-          const int n = i / vec_per_row, v = i % vec_per_row;
-          uint4 val = make_uint4(0, 0, 0, 0);
-          if (n < job.z) {
-            if (ph == 0) {
-              const int tok = p.order[job.y + n] / p.k;
-              val = __ldg(reinterpret_cast<const uint4*>(p.x + (size_t)tok * p.H) + v);
-            } else {
-              val = __ldcg(reinterpret_cast<const uint4*>(p.inter + (size_t)(job.y + n) * p.I) + v);
-            }
-          }
-          *reinterpret_cast<uint4*>(xs + n * pitch + v * 16) = val;
+  } else if (warp == SK_W_ACT) {
+    // ------------------------------------------------------------------ activation staging
+    if (lane == 0) {
+      int k = 0;  // non-empty segments so far
+      for (int s = 0; s < nseg; ++s) {
+        int ph, job;
+        long long u0, u1;
+        segs.at(s, ph, job, u0, u1);
+        if (u1 <= u0) continue;
+        const int b = k % NBUF;
+        if (k >= NBUF) mbar_wait(cb.act_empty + b, ((k / NBUF) + 1) & 1, p.timeout_ns, status);
+        const int4 jb = jobs[job];
+        const int K = ph ? p.I : p.H;
+        if (ph == 1) {
+          wait_geq(p.doneA + job, nrbA, p.timeout_ns, status);  // every phase-A unit of this job is published
+          fence_proxy_async_global();
         }
-        named_bar(1, SK_NW * 32);
-        cur = jidx;
+        uint8_t* dst = bufs + (size_t)b * L.rows * L.pitch;
+        const int ntok = min(jb.z, L.rows);
+        mbar_arrive_expect_tx(cb.act_full + b, ntok * K * 2);
+        for (int n = 0; n < ntok; ++n) {
+          const uint16_t* src = ph ? p.inter + (size_t)(jb.y + n) * p.I : p.x + (size_t)(order[jb.y + n] / p.k) * p.H;
+          bulk_g2s(dst + n * (size_t)(K * 2 + 16), src, K * 2, cb.act_full + b);
+        }
+        ++k;
       }
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      const uint8_t* xrow = xs + g * pitch;
-      for (int c = 0; c < nch; ++c, ++it) {
-        const int ns = min(SK_CS, nS - c * SK_CS);
-        const int st = it % SK_NSTAGE;
-        mbar_wait(full + st, (it / SK_NSTAGE) & 1, p.timeout_ns, status);
-        const uint8_t* stage = ring + st * SK_STAGE_BYTES;
-        for (int s = warp; s < ns; s += SK_NW) sk_slice(stage, s, xrow, c * SK_CS + s, lane, t, acc);
+      for (int i = max(0, k - NBUF); i < k; ++i) mbar_wait(cb.act_full + (i % NBUF), (i / NBUF) & 1, p.timeout_ns, status);
+      TRACE_AT(20);
+    }
+  } else if (warp == SK_W_SIG) {
+    // ------------------------------------------------------------------ signalling
+    int k = 0;
+    for (int s = 0; s < nseg; ++s) {
+      int ph, job;
+      long long u0, u1;
+      segs.at(s, ph, job, u0, u1);
+      if (u1 <= u0) continue;
+      const int slot = k % SK_SEG_RING;
+      const int want = (int)(u1 - u0);
+      // all units of the segment reduced and written by the compute warps (CTA-scope release, acquire here)
+      if (lane == 0) {
+        const uint64_t t0 = gtimer();
+        while (*reinterpret_cast<volatile int*>(&cb.seg_cnt[slot]) < want) {
+          __nanosleep(200);
+          if (gtimer() - t0 > p.timeout_ns) {
+            set_status(status, XCB_STATUS_DEVICE_TIMEOUT);
+            break;
+          }
+        }
+      }
+      __syncwarp();
+      __threadfence();  // cumulative: publishes the compute warps' epilogue writes GPU-wide before the counters move
+      if (lane == 0) {
+        cb.seg_cnt[slot] = 0;
+        *reinterpret_cast<volatile int*>(&cb.seg_gen[slot]) = k / SK_SEG_RING + 1;
+      }
+      if (ph == 0) {
+        if (lane == 0) atomicAdd(p.doneA + job, want);
+      } else if (!p.grid_combine) {
+        // one count per 16-row block; the CTA that completes a block combines it (all its threads, at the end)
+        for (long long u = u0 + lane; u < u1; u += 32) {
+          const int rb = (int)(u - (long long)job * nrbB);
+          if (atomicAdd(p.rbcnt + rb, 1) == njobs - 1) cb.list[atomicAdd(&cb.nlist, 1)] = rb;
+        }
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty + st);
       }
-      // cross-warp reduction and epilogue (warp 0)
-      float* rb_buf = red + rbuf * (SK_NW * 32 * 4);
-      *reinterpret_cast<float4*>(rb_buf + (warp * 32 + lane) * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      named_bar(1, SK_NW * 32);
-      if (warp == 0) {
+      ++k;
+    }
+    if (lane == 0) TRACE_AT(21);
+  } else if (warp == SK_W_EPI) {
+    // ------------------------------------------------------------------ reduction + epilogue
+    const int g = lane >> 2, t = lane & 3;
+    int useq = 0, k = 0;
+    for (int s = 0; s < nseg; ++s) {
+      int ph, job;
+      long long u0, u1;
+      segs.at(s, ph, job, u0, u1);
+      if (u1 <= u0) continue;
+      const int nrb = ph ? nrbB : nrbA;
+      const int4 jb = jobs[job];
+      const float gsc = gs_cached ? cb.gs[ph][job] : (ph ? p.gsB : p.gsA)[jb.x] * kTwo52;
+      for (long long u = u0; u < u1; ++u, ++useq) {
+        const int rb = (int)(u - (long long)job * nrb);
+        const int slot = useq % NSLOT;
+        mbar_wait(cb.slot_full + slot, (useq / NSLOT) & 1, p.timeout_ns, status);
+        const float* sb = red + slot * SK_SLOT_FLOATS;
         float v[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int w = 0; w < SK_NW; ++w) {
-          const float4 r = *reinterpret_cast<const float4*>(rb_buf + (w * 32 + lane) * 4);
+#pragma unroll 8
+        for (int w = 0; w < SK_NW; ++w) {  // fixed warp order: deterministic sums
+          const float4 r = *reinterpret_cast<const float4*>(sb + (w * 32 + lane) * 4);
           v[0] += r.x; v[1] += r.y; v[2] += r.z; v[3] += r.w;
         }
-        const int e = job.x;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(cb.slot_free + slot);
         if (ph == 0) {
-          const float gsc = p.gsA[e] * kTwo52;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int n = 2 * t + h;
-            if (n < job.z) {
+            if (n < jb.z) {
               const float gt = v[h] * gsc, up = v[2 + h] * gsc;
               const float hv = gt / (1.f + expf(-gt)) * up;
-              p.inter[(size_t)(job.y + n) * p.I + rb * 8 + g] = f2bf(hv);
+              p.inter[(size_t)(jb.y + n) * p.I + rb * 8 + g] = f2bf(hv);
             }
           }
-          __threadfence();
-          __syncwarp();
-          if (lane == 0) atomicAdd(p.doneA + jidx, 1);
         } else {
-          const float gsc = p.gsB[e] * kTwo52;
           const int r0 = rb * 16 + g, r1 = r0 + 8;
           float n0 = 1.f, n1 = 1.f;
           if (p.post_norm) {
@@ -217,56 +502,162 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
             const int n = 2 * t + h;
             const float y0 = v[h] * gsc * n0, y1 = v[2 + h] * gsc * n1;
             float sq = y0 * y0 + y1 * y1;
-            if (n < job.z) {
-              p.y[(size_t)(job.y + n) * p.H + r0] = y0;
-              p.y[(size_t)(job.y + n) * p.H + r1] = y1;
+            if (n < jb.z) {
+              p.y[(size_t)(jb.y + n) * p.H + r0] = y0;
+              p.y[(size_t)(jb.y + n) * p.H + r1] = y1;
             }
             if (p.post_norm) {
               sq += __shfl_xor_sync(0xffffffffu, sq, 4);
               sq += __shfl_xor_sync(0xffffffffu, sq, 8);
               sq += __shfl_xor_sync(0xffffffffu, sq, 16);
-              if (g == 0 && n < job.z) atomicAdd(p.ss + job.y + n, sq);
+              if (g == 0 && n < jb.z) atomicAdd(p.ss + jb.y + n, sq);
             }
           }
         }
+        // hand the finished unit to the signalling warp (CTA-scope release of the epilogue writes)
+        __syncwarp();
+        if (lane == 0) {
+          const int sl = k % SK_SEG_RING;
+          const int want = k / SK_SEG_RING;
+          if (*reinterpret_cast<volatile int*>(&cb.seg_gen[sl]) < want) {
+            const uint64_t t0 = gtimer();
+            while (*reinterpret_cast<volatile int*>(&cb.seg_gen[sl]) < want) {
+              __nanosleep(100);
+              if (gtimer() - t0 > p.timeout_ns) {
+                set_status(status, XCB_STATUS_DEVICE_TIMEOUT);
+                break;
+              }
+            }
+          }
+          __threadfence_block();
+          atomicAdd(&cb.seg_cnt[sl], 1);
+        }
       }
-      rbuf ^= 1;
+      ++k;
+    }
+    if (lane == 0) TRACE_AT(22);
+  } else {
+    // ------------------------------------------------------------------ compute warps
+    const int g = lane >> 2, t = lane & 3;
+    const int grow = g < L.rows ? g : L.rows - 1;  // MMA columns past the job's tokens are computed and discarded
+    int it = 0, useq = 0, k = 0;
+    for (int s = 0; s < nseg; ++s) {
+      int ph, job;
+      long long u0, u1;
+      segs.at(s, ph, job, u0, u1);
+      if (u1 <= u0) continue;
+      const int b = k % NBUF;
+      const int nS = ph ? nSB : nSA, nch = ph ? nchB : nchA;
+      const int pitch = (ph ? p.I : p.H) * 2 + 16;
+      mbar_wait(cb.act_full + b, (k / NBUF) & 1, p.timeout_ns, status);
+      const uint8_t* xrow = bufs + (size_t)b * L.rows * L.pitch + grow * pitch;
+      for (long long u = u0; u < u1; ++u, ++useq) {
+        float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c = 0; c < nch; ++c, ++it) {
+          const int ns0 = min(SK_GS, nS - 2 * c * SK_GS);
+          const int ns1 = max(0, min(SK_GS, nS - (2 * c + 1) * SK_GS));
+          const int st = it % NST;
+          mbar_wait(cb.full + st, (it / NST) & 1, p.timeout_ns, status);
+          const uint8_t* stage = ring + st * SK_STAGE_BYTES;
+          if (warp < ns0) sk_slice(stage, ns0, warp, xrow, 2 * c * SK_GS + warp, lane, t, acc0, acc1);
+          if (warp < ns1) sk_slice(stage + ns0 * 576, ns1, warp, xrow, (2 * c + 1) * SK_GS + warp, lane, t, acc0, acc1);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(cb.empty + st);
+        }
+        // ---- hand the unit's partial sums to the epilogue warp through a reduction slot
+        const int slot = useq % NSLOT;
+        if (useq >= NSLOT) mbar_wait(cb.slot_free + slot, ((useq / NSLOT) + 1) & 1, p.timeout_ns, status);
+        *reinterpret_cast<float4*>(red + slot * SK_SLOT_FLOATS + (warp * 32 + lane) * 4) =
+            make_float4(acc0[0] + acc1[0], acc0[1] + acc1[1], acc0[2] + acc1[2], acc0[3] + acc1[3]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(cb.slot_full + slot);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(cb.act_empty + b);
+      ++k;
     }
   }
 
-  // -------------------------------------------------------------------- grid barrier, combine, exit
-  named_bar(1, SK_NW * 32);
-  if (tid == 0) {
+  if (tid == 0) TRACE_AT(7);
+  // 16-row blocks this CTA completed: combine them for every token with all threads (one L2 round trip)
+  __syncthreads();
+  if (!p.grid_combine && cb.nlist > 0) {
     __threadfence();
-    atomicAdd(p.ctl + kCtlGridArrive, 1);
-    wait_geq(p.ctl + kCtlGridArrive, G, p.timeout_ns, status);
-  }
-  named_bar(1, SK_NW * 32);
-  const int nseg = (p.H + 1023) / 1024;
-  for (int item = bid; item < p.T * nseg; item += G) {
-    const int tk = item / nseg, col = (item % nseg) * 1024 + tid * 4;
-    if (col < p.H) {
-      float a[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int s = 0; s < p.k; ++s) {
-        const int q = p.pos[tk * p.k + s];
-        if (q >= 0) {
-          float r = p.wts[tk * p.k + s];
-          if (p.post_norm) r *= rsqrtf(__ldcg(p.ss + q) / (float)p.H + 1e-8f);
-          const float4 yv = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * p.H + col));
-          a[0] += r * yv.x; a[1] += r * yv.y; a[2] += r * yv.z; a[3] += r * yv.w;
+    const int nl = cb.nlist, items = nl * 16 * p.T;
+    for (int i = tid; i < items; i += SK_THREADS) {
+      const int rb = cb.list[i / (16 * p.T)], rem = i % (16 * p.T);
+      const int tk = rem / 16, row = rb * 16 + rem % 16;
+      float yv[16], wv[16];
+#pragma unroll
+      for (int s = 0; s < 16; ++s) {
+        yv[s] = 0.f;
+        wv[s] = 0.f;
+        if (s < p.k) {
+          const int q = pos[tk * p.k + s];
+          if (q >= 0) {
+            yv[s] = __ldcg(p.y + (size_t)q * p.H + row);
+            wv[s] = wts[tk * p.k + s];
+          }
         }
       }
-      uint2 o;
-      o.x = (uint32_t)f2bf(a[0]) | ((uint32_t)f2bf(a[1]) << 16);
-      o.y = (uint32_t)f2bf(a[2]) | ((uint32_t)f2bf(a[3]) << 16);
-      *reinterpret_cast<uint2*>(p.out + (size_t)tk * p.H + col) = o;
+      float a = 0.f;
+#pragma unroll
+      for (int s = 0; s < 16; ++s) a += wv[s] * yv[s];
+      p.out[(size_t)tk * p.H + row] = f2bf(a);
+    }
+    __syncthreads();
+    for (int i = tid; i < nl; i += SK_THREADS) p.rbcnt[cb.list[i]] = 0;
+  }
+  // no local route at all: no unit will combine, so the output is zero
+  if (!p.grid_combine && njobs == 0) {
+    const size_t n2 = (size_t)p.T * p.H / 2;
+    for (size_t i = (size_t)bid * SK_THREADS + tid; i < n2; i += (size_t)G * SK_THREADS)
+      reinterpret_cast<uint32_t*>(p.out)[i] = 0u;
+  }
+
+  // -------------------------------------------------------------------- grid combine (post-norm / large batch)
+  if (p.grid_combine) {
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      atomicAdd(p.ctl + kCtlGridArrive, 1);
+      wait_geq(p.ctl + kCtlGridArrive, G, p.timeout_ns, status);
+    }
+    __syncthreads();
+    const int nsegc = (p.H + 1023) / 1024;
+    for (int item = bid; item < p.T * nsegc; item += G) {
+      const int tk = item / nsegc, col = (item % nsegc) * 1024 + tid * 4;
+      if (tid < 256 && col < p.H) {
+        float a[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int s = 0; s < p.k; ++s) {
+          const int q = pos[tk * p.k + s];
+          if (q >= 0) {
+            float r = wts[tk * p.k + s];
+            if (p.post_norm) r *= rsqrtf(__ldcg(p.ss + q) / (float)p.H + 1e-8f);
+            const float4 yv = __ldcg(reinterpret_cast<const float4*>(p.y + (size_t)q * p.H + col));
+            a[0] += r * yv.x; a[1] += r * yv.y; a[2] += r * yv.z; a[3] += r * yv.w;
+          }
+        }
+        uint2 o;
+        o.x = (uint32_t)f2bf(a[0]) | ((uint32_t)f2bf(a[1]) << 16);
+        o.y = (uint32_t)f2bf(a[2]) | ((uint32_t)f2bf(a[3]) << 16);
+        *reinterpret_cast<uint2*>(p.out + (size_t)tk * p.H + col) = o;
+      }
     }
   }
-  named_bar(1, SK_NW * 32);
+
+  // -------------------------------------------------------------------- exit: the last CTA resets the counters
+  __syncthreads();
   if (tid == 0) {
+    TRACE_AT(8);
     __threadfence();
     const int done = atomicAdd(p.ctl + kCtlExit, 1);
     if (done == G - 1) {
+      if (p.small_route) {
+        for (int j = 0; j < njobs; ++j) p.doneA[j] = 0;
+        if (p.post_norm)
+          for (int q = 0; q < rt.nroutes; ++q) p.ss[q] = 0.f;
+      }
       p.ctl[kCtlGridArrive] = 0;
       p.ctl[kCtlExit] = 0;
       __threadfence();
@@ -274,31 +665,45 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
   }
 }
 
-int skinny_grid(int* grid_out, int* smem_out, int H, int I) {
+#if XCB_TRACE
+extern "C" int xcb_trace_read(void* host, size_t bytes) {
+  return cudaMemcpyFromSymbol(host, g_trace, bytes) == cudaSuccess ? 0 : 4;
+}
+extern "C" int xcb_trace_clear() {
+  static unsigned long long zero[1024 * kTraceSlots];
+  return cudaMemcpyToSymbol(g_trace, zero, sizeof(zero)) == cudaSuccess ? 0 : 4;
+}
+#endif
+
+int skinny_config(int* grid_out, int* smem_out, int H, int I, int job_tokens, int small_route) {
   static int cached_dev = -1, cached_sms = 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return XCB_ERR_CUDA;
-  const SkSmemOffsets so = sk_smem(H, I);
-  if (cudaFuncSetAttribute(skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, so.total) != cudaSuccess)
+  const SkLayout L = sk_layout(H, I, job_tokens, small_route);
+  if (L.nstage < 4) return XCB_ERR_UNSUPPORTED;
+  if (cudaFuncSetAttribute(skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) != cudaSuccess)
     return XCB_ERR_CUDA;
   if (dev != cached_dev) {
     if (cudaDeviceGetAttribute(&cached_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return XCB_ERR_CUDA;
     cached_dev = dev;
   }
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, skinny_kernel, SK_THREADS, so.total) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, skinny_kernel, SK_THREADS, L.total) != cudaSuccess ||
       per_sm < 1)
     return XCB_ERR_CUDA;
   *grid_out = cached_sms * per_sm;
-  *smem_out = so.total;
+  *smem_out = L.total;
   return XCB_OK;
 }
 
-size_t skinny_smem_bytes(int H, int I) { return (size_t)sk_smem(H, I).total; }
+size_t skinny_smem_bytes(int H, int I) {
+  const SkLayout L = sk_layout(H, I, kJobTokens, 1);
+  return L.nstage >= 4 ? (size_t)L.total : (size_t)1 << 30;
+}
 
 int launch_skinny(const SkinnyParams& p, cudaStream_t stream) {
   int grid = 0, smem = 0;
-  int rc = skinny_grid(&grid, &smem, p.H, p.I);
+  int rc = skinny_config(&grid, &smem, p.H, p.I, p.job_tokens, p.small_route);
   if (rc != XCB_OK) return rc;
   skinny_kernel<<<grid, SK_THREADS, smem, stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;

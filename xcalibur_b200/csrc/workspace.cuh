@@ -11,15 +11,20 @@ namespace xcb {
 
 constexpr int kJobTokens = 8;  // tokens per decode-path job (one m16n8k16 n-tile)
 
-// Control words at the start of the workspace.
+// Fixed header at the start of the workspace (same offsets whatever the call's size).
 enum CtlWord : int {
   kCtlStatus = 0,      // XCB_STATUS_* bits
   kCtlGridArrive = 1,  // grid barrier of the decode-path kernel
   kCtlExit = 2,        // CTAs that finished the decode-path kernel (the last one resets the counters)
   kCtlJobs = 3,        // number of jobs written by the router
   kCtlRoutes = 4,      // number of local routes
-  kCtlWords = 64
+  kCtlDoneA = 64,      // [256] per-job phase-A counters when the decode kernel routes in-kernel
+  kCtlSS = 320,        // [256] fp32 per-route sums of squares (post-norm) when routing in-kernel
+  kCtlRowBlock = 576,  // [512] per-16-row-block phase-B arrival counters (H <= 8192)
+  kCtlWords = 1280
 };
+constexpr int kSmallRoutes = 256;  // T*k up to which the decode kernel routes in-kernel (one launch per call)
+constexpr int kSmallTokens = 32;
 
 struct WsLayout {
   size_t ctl, ids, wts, pos, order, counts, offsets, jobs, doneA, ss, inter, y, total;

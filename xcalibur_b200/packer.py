@@ -10,8 +10,10 @@ Decode-path ("skinny") layout of one expert matrix W [R rows, K] (K % 256 == 0, 
 * Rows are taken in *packed order*: for gate_up, 16-row block ``rb`` holds gate rows 8rb..8rb+7 then up rows
   8rb..8rb+7 (so one mma.sync accumulator lane owns the gate and the up value of the same intermediate
   feature); for down, rows stay in order.
-* A block is one *unit* of ``9*K`` bytes: codes ``[K/64 slices][32 lanes][4 steps]`` u32 (8K bytes), then
-  scale codes ``[K/256][32 lanes][4 slices][2 row halves]`` bytes (K bytes).
+* A block is one *unit* of ``9*K`` bytes, cut into groups of 16 slices (64 k each); a group of ``ns`` slices holds
+  its codes ``[ns slices][32 lanes][4 steps]`` u32 (``ns * 512`` bytes) followed by its scale codes
+  ``[ns/4][32 lanes][4 slices][2 row halves]`` bytes (``ns * 64``), so two consecutive groups (18 KB) are one
+  contiguous bulk copy.
 * Lane L = 4g + t, slice S, step j holds the 8 codes of rows {g, g+8} at k = 64S + 16t + 4j + {0,1,2,3}.
   All 16 k of a lane's slice share one 16-wide scale block (4S + t), so one scale pair serves four steps.
   The activation operand of that step is x[token][64S + 16t + 4j + 0..3]: 16 consecutive k per lane and slice.
