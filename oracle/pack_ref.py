@@ -59,12 +59,13 @@ def _apply_T(words: np.ndarray) -> np.ndarray:
 
 
 def join_units(code_bytes: np.ndarray, scale_bytes: np.ndarray) -> np.ndarray:
-    """[nb, nS*512] codes + [nb, nS*64] scales -> [nb, 9K] units: per group of 16 slices, its codes then its scales."""
+    """[nb, nS*512] codes + [nb, nS*64] scales -> [nb, 9K] units: per group of gs slices, its codes then its scales."""
     nb = code_bytes.shape[0]
     nS = code_bytes.shape[1] // 512
+    gs = packer.group_slices(64 * nS)
     parts = []
-    for g0 in range(0, nS, 16):
-        ns = min(16, nS - g0)
+    for g0 in range(0, nS, gs):
+        ns = gs
         parts.append(code_bytes[:, g0 * 512:(g0 + ns) * 512])
         parts.append(scale_bytes[:, g0 * 64:(g0 + ns) * 64])
     return np.concatenate(parts, axis=1).reshape(nb, -1)
@@ -73,10 +74,11 @@ def join_units(code_bytes: np.ndarray, scale_bytes: np.ndarray) -> np.ndarray:
 def split_units(units: np.ndarray, K: int):
     """Inverse of join_units: [nb, 9K] -> ([nb, nS*512] codes, [nb, nS*64] scales)."""
     nS = K // 64
+    gs = packer.group_slices(K)
     cs, ss = [], []
     off = 0
-    for g0 in range(0, nS, 16):
-        ns = min(16, nS - g0)
+    for g0 in range(0, nS, gs):
+        ns = gs
         cs.append(units[:, off:off + ns * 512])
         ss.append(units[:, off + ns * 512:off + ns * 576])
         off += ns * 576

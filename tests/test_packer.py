@@ -7,7 +7,7 @@ from xcalibur_b200 import packer
 
 
 @pytest.mark.parametrize("gate_up", [False, True])
-@pytest.mark.parametrize("R,K", [(32, 256), (16, 768), (48, 1024)])
+@pytest.mark.parametrize("R,K", [(32, 256), (16, 768), (48, 1024), (16, 1280), (16, 3072)])
 def test_pack_roundtrip_exact(gate_up, R, K):
     rng = np.random.default_rng(R * 7 + K)
     w = rng.standard_normal((1, R, K)).astype(np.float32) * np.float32(0.02)

@@ -11,7 +11,8 @@ import ctypes
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libxcb_moe.so")
+# the in-tree build; XCB_MOE_LIB selects another build of the same library (e.g. one compiled with other tile knobs)
+LIB_PATH = os.environ.get("XCB_MOE_LIB") or os.path.join(HERE, "libxcb_moe.so")
 
 XCB_OK = 0
 XCB_ERR_INVALID_ARG = 1

@@ -112,7 +112,7 @@ __device__ __forceinline__ void named_bar(int id, int threads) {
 // D = A(16x16 bf16, row) * B(16x8 bf16, col) + D, fp32 accumulate.
 __device__ __forceinline__ void mma_16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                           uint32_t b1) {
-  asm volatile(
+  asm(  // not volatile: no side effects, so the compiler may interleave it with the decode of other words
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));

@@ -6,6 +6,13 @@
 
 namespace xcb {
 
+// Slices (64 k each) per group of the packed decode-path layout for a reduction length K (K % 256 == 0): the
+// largest of 16, 12, 8, 4 that divides K / 64, so every unit is a whole number of equal groups.
+__host__ __device__ inline int group_slices(int K) {
+  const int n = K / 64;
+  return n % 16 == 0 ? 16 : (n % 12 == 0 ? 12 : (n % 8 == 0 ? 8 : 4));
+}
+
 struct RouteParams {
   const float* logits;     // [T, E_tot] or null
   const int* ids_in;       // [T, k] or null

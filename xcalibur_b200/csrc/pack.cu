@@ -61,9 +61,9 @@ __global__ void pack_codes_kernel(PackParams p) {
     const uint32_t word = (uint32_t)fold_byte(c0[bidx], f0) | ((uint32_t)fold_byte(c1[bidx], f1) << 8) |
                           ((uint32_t)fold_byte(c0[bidx + 1], f0) << 16) | ((uint32_t)fold_byte(c1[bidx + 1], f1) << 24);
     const uint32_t packed = tab[0][word & 255] ^ tab[1][(word >> 8) & 255] ^ tab[2][(word >> 16) & 255] ^ tab[3][word >> 24];
-    // unit = groups of 16 slices, each group's codes followed by its scale codes (one bulk copy per group pair)
-    const int grp = S >> 4, s = S & 15;
-    uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + ub * (size_t)9 * p.K + (size_t)grp * 9216) + s * 128 + lane * 4 + j;
+    // unit = groups of gs slices, each group's codes followed by its scale codes
+    const int gs = group_slices(p.K), grp = S / gs, s = S % gs;
+    uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + ub * (size_t)9 * p.K + (size_t)grp * gs * 576) + s * 128 + lane * 4 + j;
     *dst = packed;
   }
 }
@@ -84,9 +84,8 @@ __global__ void pack_scales_kernel(PackParams p) {
     const int blk = 4 * (4 * S4 + s4) + t;
     int f;
     const uint32_t c = scale_code(p.sf[((size_t)e * p.R + ro) * K16 + blk], f);
-    const int S = 4 * S4 + s4, grp = S >> 4, s = S & 15;
-    const int ns = min(16, p.K / 64 - 16 * grp);
-    p.out[ub * (size_t)9 * p.K + (size_t)grp * 9216 + (size_t)ns * 512 + (s >> 2) * 256 + lane * 8 + (s & 3) * 2 + h] =
+    const int gs = group_slices(p.K), S = 4 * S4 + s4, grp = S / gs, s = S % gs;
+    p.out[ub * (size_t)9 * p.K + (size_t)grp * gs * 576 + (size_t)gs * 512 + (s >> 2) * 256 + lane * 8 + (s & 3) * 2 + h] =
         (uint8_t)c;
   }
 }

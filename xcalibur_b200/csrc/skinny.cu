@@ -41,20 +41,28 @@ constexpr int kTraceSlots = 32;
 __device__ unsigned long long g_trace[1024 * kTraceSlots];
 #define TRACE_AT(slot) (g_trace[blockIdx.x * kTraceSlots + (slot)] = gtimer())
 #define TRACE_ADD(slot, v) atomicAdd(&g_trace[blockIdx.x * kTraceSlots + (slot)], (unsigned long long)(v))
+#define TRACE_GET(slot) (*(volatile unsigned long long*)&g_trace[blockIdx.x * kTraceSlots + (slot)])
 #else
 #define TRACE_AT(slot) ((void)0)
 #define TRACE_ADD(slot, v) ((void)0)
 #endif
 
-constexpr int SK_NW = 16;                               // compute warps
+#ifndef XCB_SK_NW
+#define XCB_SK_NW 16
+#endif
+constexpr int SK_NW = XCB_SK_NW;                        // compute warps (each takes slices w, w + SK_NW, ... of a group)
 constexpr int SK_W_PROD = SK_NW;                        // weight producer warp
 constexpr int SK_W_ACT = SK_NW + 1;                     // activation staging warp
 constexpr int SK_W_SIG = SK_NW + 2;                     // signalling warp
-constexpr int SK_W_EPI = SK_NW + 3;                     // reduction + epilogue warp
-constexpr int SK_THREADS = (SK_NW + 4) * 32;
-constexpr int SK_GS = 16;                               // slices (64 k) per group = one per compute warp
-constexpr int SK_GROUP_BYTES = SK_GS * 576;             // 8 KB codes + 1 KB scale codes
-constexpr int SK_STAGE_BYTES = 2 * SK_GROUP_BYTES;      // a stage is two groups: one 18 KB bulk copy
+constexpr int SK_W_EPI = SK_NW + 3;                     // reduction + epilogue warps (SK_NEPI of them)
+constexpr int SK_NEPI = 2;                              // epilogue warp e takes the units with useq % SK_NEPI == e
+constexpr int SK_THREADS = (SK_NW + 3 + SK_NEPI) * 32;
+constexpr int SK_SLICE_BYTES = 576;                     // 512 B of codes + 64 B of scale codes per 64-k slice
+#ifndef XCB_SK_PER
+#define XCB_SK_PER 2
+#endif
+constexpr int SK_PER = XCB_SK_PER;                      // slices per compute warp per stage
+constexpr int SK_STAGE_SLICES = SK_PER * SK_NW;         // slices per full stage (18 KB at 2 x 16)
 constexpr int SK_MAX_STAGES = 16;
 constexpr int SK_MAX_SLOTS = 4;                         // reduction slots
 constexpr int SK_SLOT_FLOATS = SK_NW * 32 * 4;
@@ -92,7 +100,7 @@ struct SkCtl {
 };
 
 struct SkLayout {
-  int buf, red, route, ctl, ring, total, nstage, nbuf, nslot, rows, pitch;
+  int buf, red, route, ctl, ring, total, nstage, nbuf, nslot, rows, pitch, stage_slices;
 };
 
 __host__ __device__ inline SkLayout sk_layout(int H, int I, int job_tokens, int small_route) {
@@ -102,19 +110,23 @@ __host__ __device__ inline SkLayout sk_layout(int H, int I, int job_tokens, int 
   if (o.rows < 1) o.rows = 1;
   const int route = small_route ? (int)sizeof(SkRoute) : 0;
   o.nstage = 0;
-  for (int nbuf = SK_MAX_BUFS; nbuf >= 1; --nbuf) {
-    for (int nslot = SK_MAX_SLOTS; nslot >= 2; nslot /= 2) {
-      o.nbuf = nbuf;
-      o.nslot = nslot;
-      o.buf = 0;
-      o.red = o.buf + nbuf * o.rows * o.pitch;
-      o.route = o.red + nslot * SK_SLOT_FLOATS * 4;
-      o.ctl = (o.route + route + 15) & ~15;
-      o.ring = (o.ctl + (int)sizeof(SkCtl) + 1023) & ~1023;
-      const int ns = (SK_SMEM_LIMIT - o.ring) / SK_STAGE_BYTES;
-      o.nstage = ns > SK_MAX_STAGES ? SK_MAX_STAGES : ns;
-      o.total = o.ring + o.nstage * SK_STAGE_BYTES;
-      if (o.nstage >= 6) return o;
+  // full-size stages when at least 4 fit, else half-size stages
+  for (int ss = SK_STAGE_SLICES; ss >= SK_STAGE_SLICES / 2; ss /= 2) {
+    for (int nbuf = SK_MAX_BUFS; nbuf >= 1; --nbuf) {
+      for (int nslot = SK_MAX_SLOTS; nslot >= 2; nslot /= 2) {
+        o.stage_slices = ss;
+        o.nbuf = nbuf;
+        o.nslot = nslot;
+        o.buf = 0;
+        o.red = o.buf + nbuf * o.rows * o.pitch;
+        o.route = o.red + nslot * SK_SLOT_FLOATS * 4;
+        o.ctl = (o.route + route + 15) & ~15;
+        o.ring = (o.ctl + (int)sizeof(SkCtl) + 1023) & ~1023;
+        const int ns = (SK_SMEM_LIMIT - o.ring) / (ss * SK_SLICE_BYTES);
+        o.nstage = ns > SK_MAX_STAGES ? SK_MAX_STAGES : ns;
+        o.total = o.ring + o.nstage * ss * SK_SLICE_BYTES;
+        if (o.nstage >= 4) return o;
+      }
     }
   }
   return o;
@@ -323,7 +335,8 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
   const float* wts = p.small_route ? rt.wts : p.wts;
   const int nrbA = (2 * p.I) / 16, nrbB = p.H / 16;
   const int nSA = p.H / 64, nSB = p.I / 64;  // slices per unit
-  const int nchA = ((nSA + SK_GS - 1) / SK_GS + 1) / 2, nchB = ((nSB + SK_GS - 1) / SK_GS + 1) / 2;  // stages/unit
+  const int gsA = group_slices(p.H), gsB = group_slices(p.I);
+  const int ssA = L.stage_slices / gsA * gsA, ssB = L.stage_slices / gsB * gsB;  // slices per full stage (whole groups)
   const size_t unitA = (size_t)9 * p.H, unitB = (size_t)9 * p.I;
   SkSegments segs;
   segs.init(njobs, nrbA, nrbB, G, bid, njobs <= SK_WAVE_JOBS);
@@ -365,22 +378,21 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
               bulk_prefetch_l2(first + off, (uint32_t)min(total - off, (size_t)1 << 20));
           }
         }
-        const int nrb = ph ? nrbB : nrbA, nS = ph ? nSB : nSA, nch = ph ? nchB : nchA;
-        const uint8_t* wbase = ph ? p.wB : p.wA;
-        const size_t ub = ph ? unitB : unitA;
-        const int e = jobs[job].x;
-        for (long long u = u0; u < u1 && ok; ++u) {
-          const uint8_t* unit = wbase + ((size_t)e * nrb + (size_t)(u - (long long)job * nrb)) * ub;
-          for (int c = 0; c < nch; ++c, ++it) {
-            const int ns = min(2 * SK_GS, nS - c * 2 * SK_GS);
-            const int st = it % NST;
-            if (it >= NST && !mbar_wait(cb.empty + st, ((it / NST) + 1) & 1, p.timeout_ns, status)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(cb.full + st, ns * 576);
-            bulk_g2s_stream(ring + st * SK_STAGE_BYTES, unit + (size_t)c * SK_STAGE_BYTES, ns * 576, cb.full + st, pol);
+        // the segment's units are one contiguous byte range; stream it in stages of whole groups
+        const int nrb = ph ? nrbB : nrbA, ss = ph ? ssB : ssA;
+        const long long nsl = (u1 - u0) * (ph ? nSB : nSA);
+        const uint8_t* seg = (ph ? p.wB : p.wA) +
+                             ((size_t)jobs[job].x * nrb + (size_t)(u0 - (long long)job * nrb)) * (ph ? unitB : unitA);
+        for (long long base = 0; base < nsl && ok; base += ss, ++it) {
+          const int ns = (int)min((long long)ss, nsl - base);
+          const int st = it % NST;
+          if (it >= NST && !mbar_wait(cb.empty + st, ((it / NST) + 1) & 1, p.timeout_ns, status)) {
+            ok = false;
+            break;
           }
+          mbar_arrive_expect_tx(cb.full + st, ns * SK_SLICE_BYTES);
+          bulk_g2s_stream(ring + (size_t)st * L.stage_slices * SK_SLICE_BYTES, seg + (size_t)base * SK_SLICE_BYTES,
+                          ns * SK_SLICE_BYTES, cb.full + st, pol);
         }
       }
       TRACE_AT(3);
@@ -455,9 +467,10 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
       ++k;
     }
     if (lane == 0) TRACE_AT(21);
-  } else if (warp == SK_W_EPI) {
+  } else if (warp >= SK_W_EPI) {
     // ------------------------------------------------------------------ reduction + epilogue
     const int g = lane >> 2, t = lane & 3;
+    const int epi = warp - SK_W_EPI;
     int useq = 0, k = 0;
     for (int s = 0; s < nseg; ++s) {
       int ph, job;
@@ -468,6 +481,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
       const int4 jb = jobs[job];
       const float gsc = gs_cached ? cb.gs[ph][job] : (ph ? p.gsB : p.gsA)[jb.x] * kTwo52;
       for (long long u = u0; u < u1; ++u, ++useq) {
+        if (useq % SK_NEPI != epi) continue;
         const int rb = (int)(u - (long long)job * nrb);
         const int slot = useq % NSLOT;
         mbar_wait(cb.slot_full + slot, (useq / NSLOT) & 1, p.timeout_ns, status);
@@ -486,7 +500,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
             const int n = 2 * t + h;
             if (n < jb.z) {
               const float gt = v[h] * gsc, up = v[2 + h] * gsc;
-              const float hv = gt / (1.f + expf(-gt)) * up;
+              const float hv = __fdividef(gt, 1.f + __expf(-gt)) * up;  // SiLU(g) * u (fast exp / divide)
               p.inter[(size_t)(jb.y + n) * p.I + rb * 8 + g] = f2bf(hv);
             }
           }
@@ -538,39 +552,78 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
     if (lane == 0) TRACE_AT(22);
   } else {
     // ------------------------------------------------------------------ compute warps
+    // A segment's slices are streamed in stages of whole groups; warp w takes stage slices w, w + SK_NW, ...
+    // Each slice belongs to one unit (its 16 rows); a warp hands its partial sums of a unit to the epilogue warps
+    // when its slices move past the unit (a unit none of whose slices this warp saw gets a zero partial).
     const int g = lane >> 2, t = lane & 3;
     const int grow = g < L.rows ? g : L.rows - 1;  // MMA columns past the job's tokens are computed and discarded
-    int it = 0, useq = 0, k = 0;
+    int st = 0, useq = 0, k = 0;
+    uint32_t sphase = 0;
+    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+    float a2[4] = {0.f, 0.f, 0.f, 0.f}, a3[4] = {0.f, 0.f, 0.f, 0.f};
+    auto flush = [&]() {  // deposit this warp's partial of unit `useq` and start the next unit
+      const int slot = useq % NSLOT;
+      if (useq >= NSLOT) mbar_wait(cb.slot_free + slot, ((useq / NSLOT) + 1) & 1, p.timeout_ns, status);
+      *reinterpret_cast<float4*>(red + slot * SK_SLOT_FLOATS + (warp * 32 + lane) * 4) =
+          make_float4(a0[0] + a2[0] + (a1[0] + a3[0]), a0[1] + a2[1] + (a1[1] + a3[1]),
+                      a0[2] + a2[2] + (a1[2] + a3[2]), a0[3] + a2[3] + (a1[3] + a3[3]));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(cb.slot_full + slot);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a0[i] = a1[i] = a2[i] = a3[i] = 0.f;
+      ++useq;
+    };
     for (int s = 0; s < nseg; ++s) {
       int ph, job;
       long long u0, u1;
       segs.at(s, ph, job, u0, u1);
       if (u1 <= u0) continue;
       const int b = k % NBUF;
-      const int nS = ph ? nSB : nSA, nch = ph ? nchB : nchA;
+      const int spu = ph ? nSB : nSA, gs = ph ? gsB : gsA, ss = ph ? ssB : ssA;
       const int pitch = (ph ? p.I : p.H) * 2 + 16;
+      const long long nsl = (u1 - u0) * spu;
       mbar_wait(cb.act_full + b, (k / NBUF) & 1, p.timeout_ns, status);
       const uint8_t* xrow = bufs + (size_t)b * L.rows * L.pitch + grow * pitch;
-      for (long long u = u0; u < u1; ++u, ++useq) {
-        float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int c = 0; c < nch; ++c, ++it) {
-          const int ns0 = min(SK_GS, nS - 2 * c * SK_GS);
-          const int ns1 = max(0, min(SK_GS, nS - (2 * c + 1) * SK_GS));
-          const int st = it % NST;
-          mbar_wait(cb.full + st, (it / NST) & 1, p.timeout_ns, status);
-          const uint8_t* stage = ring + st * SK_STAGE_BYTES;
-          if (warp < ns0) sk_slice(stage, ns0, warp, xrow, 2 * c * SK_GS + warp, lane, t, acc0, acc1);
-          if (warp < ns1) sk_slice(stage + ns0 * 576, ns1, warp, xrow, (2 * c + 1) * SK_GS + warp, lane, t, acc0, acc1);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(cb.empty + st);
+      // per-warp constants of the segment: where each of its stage slices sits (group offset, slice in group)
+      int goff[SK_PER], gsl[SK_PER];
+#pragma unroll
+      for (int j = 0; j < SK_PER; ++j) {
+        const int i = warp + j * SK_NW, q = i / gs;
+        goff[j] = q * gs * SK_SLICE_BYTES;
+        gsl[j] = i - q * gs;
+      }
+      const int nsl32 = (int)nsl;
+      int ucur = 0, uend = spu;  // unit this warp is accumulating, and the segment slice where it ends
+      for (int base = 0; base < nsl32; base += ss) {
+        mbar_wait(cb.full + st, sphase, p.timeout_ns, status);
+        const uint8_t* stage = ring + (size_t)st * L.stage_slices * SK_SLICE_BYTES;
+        const int ns = min(ss, nsl32 - base);
+#pragma unroll
+        for (int j = 0; j < SK_PER; ++j) {
+          const int i = warp + j * SK_NW;
+          if (i < ns) {
+            const int gi = base + i;
+            while (gi >= uend) {
+              flush();
+              ++ucur;
+              uend += spu;
+            }
+            if (j & 1)
+              sk_slice(stage + goff[j], gs, gsl[j], xrow, gi - (uend - spu), lane, t, a2, a3);
+            else
+              sk_slice(stage + goff[j], gs, gsl[j], xrow, gi - (uend - spu), lane, t, a0, a1);
+          }
         }
-        // ---- hand the unit's partial sums to the epilogue warp through a reduction slot
-        const int slot = useq % NSLOT;
-        if (useq >= NSLOT) mbar_wait(cb.slot_free + slot, ((useq / NSLOT) + 1) & 1, p.timeout_ns, status);
-        *reinterpret_cast<float4*>(red + slot * SK_SLOT_FLOATS + (warp * 32 + lane) * 4) =
-            make_float4(acc0[0] + acc1[0], acc0[1] + acc1[1], acc0[2] + acc1[2], acc0[3] + acc1[3]);
         __syncwarp();
-        if (lane == 0) mbar_arrive(cb.slot_full + slot);
+        if (lane == 0) mbar_arrive(cb.empty + st);
+        if (++st == NST) {
+          st = 0;
+          sphase ^= 1;
+        }
+      }
+      while (ucur < (int)(u1 - u0)) {
+        flush();
+        ++ucur;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(cb.act_empty + b);

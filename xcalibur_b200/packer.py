@@ -10,10 +10,11 @@ Decode-path ("skinny") layout of one expert matrix W [R rows, K] (K % 256 == 0, 
 * Rows are taken in *packed order*: for gate_up, 16-row block ``rb`` holds gate rows 8rb..8rb+7 then up rows
   8rb..8rb+7 (so one mma.sync accumulator lane owns the gate and the up value of the same intermediate
   feature); for down, rows stay in order.
-* A block is one *unit* of ``9*K`` bytes, cut into groups of 16 slices (64 k each); a group of ``ns`` slices holds
-  its codes ``[ns slices][32 lanes][4 steps]`` u32 (``ns * 512`` bytes) followed by its scale codes
-  ``[ns/4][32 lanes][4 slices][2 row halves]`` bytes (``ns * 64``), so two consecutive groups (18 KB) are one
-  contiguous bulk copy.
+* A block is one *unit* of ``9*K`` bytes, cut into equal groups of ``gs = group_slices(K)`` slices (64 k each;
+  16 when K/64 is a multiple of 16, else 12, 8 or 4); a group holds its codes ``[gs slices][32 lanes][4 steps]``
+  u32 (``gs * 512`` bytes) followed by its scale codes ``[gs/4][32 lanes][4 slices][2 row halves]`` bytes
+  (``gs * 64``).  Consecutive units of one expert are contiguous, so the kernel streams any run of them as
+  fixed-size bulk copies of whole groups.
 * Lane L = 4g + t, slice S, step j holds the 8 codes of rows {g, g+8} at k = 64S + 16t + 4j + {0,1,2,3}.
   All 16 k of a lane's slice share one 16-wide scale block (4S + t), so one scale pair serves four steps.
   The activation operand of that step is x[token][64S + 16t + 4j + 0..3]: 16 consecutive k per lane and slice.
@@ -165,6 +166,12 @@ def scale_code_value(c: int) -> float:
 
 
 # --------------------------------------------------------------------------------------------- sizes
+def group_slices(K: int) -> int:
+    """Slices per group for reduction length K (mirrors group_slices in the CUDA sources)."""
+    n = K // 64
+    return 16 if n % 16 == 0 else 12 if n % 12 == 0 else 8 if n % 8 == 0 else 4
+
+
 def unit_bytes(K: int) -> int:
     return 9 * K
 
