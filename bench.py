@@ -314,7 +314,8 @@ def finish(a, cfg, world, ms, kern_ms, e2e_ms, u_avg, P, clk, cpu):
         "e2e": None if e2e_ms is None else {
             "value": round(T * world / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
             "h2d_bytes_per_step": T * H * 2 + T * E * 4, "d2h_bytes_per_step": T * H * 2},
-        "gpu_launches": 2 * a.steps,
+        # one launch per step when the decode kernel routes in-kernel (T * k <= 256, T <= 32), else router + experts
+        "gpu_launches": a.steps * (1 if T * k <= 256 and T <= 32 else 2),
         "clocks": clk,
     }
     if cpu is not None:
