@@ -287,7 +287,7 @@ def finish(a, cfg, world, ms, kern_ms, e2e_ms, u_avg, P, clk, cpu):
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "peak_source": src + " (sustained)"}
     roof["traffic"] = load_traffic(cfg["workload"])
-    roof["kernel"] = "skinny_kernel"
+    roof["kernel"] = "skinny_kernel" if T * k <= 256 and T <= 32 else "gather + wide_kernel x2 + combine"
     roof["kernel_ms"] = round(kern_ms, 5)
     roof["algorithmic_bytes"] = int(alg_bytes)
     roof["algorithmic_flops"] = int(flops)
@@ -314,8 +314,9 @@ def finish(a, cfg, world, ms, kern_ms, e2e_ms, u_avg, P, clk, cpu):
         "e2e": None if e2e_ms is None else {
             "value": round(T * world / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
             "h2d_bytes_per_step": T * H * 2 + T * E * 4, "d2h_bytes_per_step": T * H * 2},
-        # one launch per step when the decode kernel routes in-kernel (T * k <= 256, T <= 32), else router + experts
-        "gpu_launches": a.steps * (1 if T * k <= 256 and T <= 32 else 2),
+        # decode kernel routing in-kernel (T * k <= 256, T <= 32): 1 launch per step; otherwise the prefill path:
+        # router, gather, two grouped GEMMs, combine
+        "gpu_launches": a.steps * (1 if T * k <= 256 and T <= 32 else 5),
         "clocks": clk,
     }
     if cpu is not None:

@@ -38,6 +38,8 @@ extern "C" {
 
 /* ---- forward flags ---- */
 #define XCB_FLAG_POST_NORM 1        /* reference contract: y *= (1 + post_norm_w); out = sum w * y / rms(y) */
+#define XCB_FLAG_DECODE_PATH 2      /* force the decode kernel (default below 257 routes and 33 tokens)       */
+#define XCB_FLAG_PREFILL_PATH 4     /* force the prefill path: tcgen05 grouped GEMMs (default above)         */
 
 /* Shape of one prepared layer.  total_experts is the router width (logits columns, valid topk ids);
  * experts [expert_offset, expert_offset + num_experts) are held in the packed buffers (the reference's
@@ -82,7 +84,8 @@ const char* xcb_status_str(int code);
 /* XCB_OK if the kernels support this shape (hidden and inter multiples of 256, hidden <= 8192, ...). */
 int xcb_moe_check_shape(const XcbMoeShape* shape);
 
-/* Bytes of one packed tensor: which = 0 gate_up [E, 2I, H], 1 down [E, H, I].
+/* Bytes of one packed tensor: which = 0 gate_up [E, 2I, H], 1 down [E, H, I].  The buffer holds two layouts of
+ * the same weights: the decode-path layout (first half) and the prefill-path layout (second half).
  * Replaces the reference's packed copies built in prepare() (moe_w4a16.py:3292-3351). */
 size_t xcb_moe_packed_bytes(const XcbMoeShape* shape, int which);
 

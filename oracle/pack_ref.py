@@ -164,3 +164,64 @@ def unpack_matrix_values(units: np.ndarray, R: int, K: int, gate_up: bool) -> np
 
 def dequantize_no_gs(codes: np.ndarray, sf: np.ndarray) -> np.ndarray:
     return nvfp4.dequantize(codes, sf, np.float32(1.0))
+
+
+# ------------------------------------------------------------------------------------------------ prefill layout
+def wide_row_order(R: int, gate_up: bool) -> np.ndarray:
+    """Original row of each wide-layout packed row: per 128-row block, gate 0-31 / up 0-31 / gate 32-63 / up 32-63
+    of the block's 64 features for gate_up; identity for down."""
+    if not gate_up:
+        return np.arange(R)
+    inter = R // 2
+    b = np.arange(R // 128)[:, None, None]
+    q = np.arange(4)[None, :, None]
+    i = np.arange(32)[None, None, :]
+    f = 64 * b + 32 * (q // 2) + i
+    return (f + inter * (q % 2)).reshape(-1)
+
+
+def pack_matrix_wide(codes: np.ndarray, sf: np.ndarray, gate_up: bool) -> np.ndarray:
+    """One expert matrix (codes [R, K/2], sf [R, K/16]) -> prefill-layout bytes [R/128 blocks, 9K/16 * 128]."""
+    R, K2 = codes.shape
+    K = 2 * K2
+    rows = wide_row_order(R, gate_up)
+    c, sc = canonical(codes[rows], sf[rows])
+    nb, ns = R // 128, K // 256
+    # natural word w of a row = its code bytes 4w..4w+3 (k = 8w..8w+7), k = 256 s + 64 chunk + 32 j + 8 w'
+    words = np.ascontiguousarray(c).view("<u4").reshape(nb, 128, ns, 4, 2, 4)   # b, row, s, chunk, j, w'
+    words = _apply_T(words)
+    code_part = np.ascontiguousarray(words.transpose(0, 2, 3, 4, 1, 5)).view(np.uint8).reshape(nb, ns, 4, 4096)
+    scale_part = np.ascontiguousarray(sc.reshape(nb, 128, ns, 4, 4).transpose(0, 2, 3, 1, 4)).reshape(nb, ns, 4, 512)
+    return np.concatenate([code_part, scale_part], axis=3).reshape(nb, -1)
+
+
+def pack_tensor_wide(codes: np.ndarray, sf: np.ndarray, gate_up: bool) -> np.ndarray:
+    """[E, R, K/2] + [E, R, K/16] -> flat packed bytes in the prefill-path layout."""
+    return np.concatenate([pack_matrix_wide(codes[e], sf[e], gate_up).reshape(-1) for e in range(codes.shape[0])])
+
+
+def unpack_matrix_wide_values(blocks: np.ndarray, R: int, K: int, gate_up: bool) -> np.ndarray:
+    """Decode prefill-layout bytes back to fp32 weights (without gs) in the ORIGINAL row order, the way the
+    kernel's dequantising threads do: run D on every word, register i half h is k = 8w + 2i + h."""
+    nb, ns = R // 128, K // 256
+    b = np.ascontiguousarray(blocks).reshape(nb, ns, 4, 4608)
+    words = np.ascontiguousarray(b[..., :4096]).view(np.uint32).reshape(nb, ns, 4, 2, 128, 4)  # b, s, c, j, row, w'
+    scodes = b[..., 4096:].reshape(nb, ns, 4, 128, 4)                                          # b, s, c, row, blk
+    M = packer.FIELD_MASK
+    q = words.astype(np.uint64)
+    rotl = lambda v, s: ((v << s) | (v >> (32 - s))) & 0xFFFFFFFF
+    u6 = (q << 6) & 0xFFFFFFFF
+    regs = [q & M, (q << 4) & M, (u6 ^ rotl(q, 10)) & M, (u6 ^ rotl(q, 12)) & M]
+    svals = np.array([packer.scale_code_value(v) for v in range(256)], dtype=np.float32)[scodes]  # b, s, c, row, blk
+    out = np.zeros((nb, 128, ns, 4, 2, 4, 8), dtype=np.float32)      # b, row, s, c, j, w', k-in-word
+    for i, r in enumerate(regs):
+        for hh in range(2):
+            bits = ((r >> (16 * hh)) & 0xFFFF).astype(np.uint32) << 16
+            val = bits.view(np.float32) * np.float32(2.0 ** 126)   # b, s, c, j, row, w'
+            out[..., 2 * i + hh] = val.transpose(0, 4, 1, 2, 3, 5)
+    blk = np.array([[2 * j + w // 2 for w in range(4)] for j in range(2)])                        # j, w'
+    sv = svals.transpose(0, 3, 1, 2, 4)[:, :, :, :, blk]                                          # b, row, s, c, j, w'
+    vals = (out * sv[..., None]).reshape(R, K)
+    orig = np.empty_like(vals)
+    orig[wide_row_order(R, gate_up)] = vals
+    return orig

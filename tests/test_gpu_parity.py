@@ -9,6 +9,7 @@ import pytest
 import torch
 
 from oracle import moe_ref, nvfp4, pack_ref
+from xcalibur_b200 import packer
 from tests._util import assert_close_bf16, bf16_bits, oracle_layer, to_np
 
 pytestmark = pytest.mark.gpu
@@ -64,8 +65,13 @@ def test_packer_bit_exact(dev):
     s13[0, 0, 0], s13[1, 3, 2], s13[2, 9, 5], s2[0, 1, 1], s2[2, 4, 0] = 0x00, 0x05, 0xB0, 0x80, 0x7E
     layer = PreparedMoE(*_weights_from_np((c13, s13, g13, c2, s2, g2), dev).values())
     torch.cuda.synchronize()
-    assert np.array_equal(to_np(layer.gate_up), pack_ref.pack_tensor(c13, s13, True))
-    assert np.array_equal(to_np(layer.down), pack_ref.pack_tensor(c2, s2, False))
+    gu, dn = to_np(layer.gate_up), to_np(layer.down)
+    assert gu.size == 2 * packer.skinny_bytes(E, 2 * I, H) and dn.size == 2 * packer.skinny_bytes(E, H, I)
+    # decode-path layout, then the prefill-path layout of the same weights
+    assert np.array_equal(gu[:gu.size // 2], pack_ref.pack_tensor(c13, s13, True))
+    assert np.array_equal(dn[:dn.size // 2], pack_ref.pack_tensor(c2, s2, False))
+    assert np.array_equal(gu[gu.size // 2:], pack_ref.pack_tensor_wide(c13, s13, True))
+    assert np.array_equal(dn[dn.size // 2:], pack_ref.pack_tensor_wide(c2, s2, False))
 
 
 def test_packer_rejects_nan_scale(dev):
@@ -237,7 +243,7 @@ def test_deepseek_decode_parity(dev, T):
     assert_close_bf16(out, oracle_layer(x, weights, want_ids, want_w))
 
 
-@pytest.mark.parametrize("T", [1, 8, 64])
+@pytest.mark.parametrize("T", [1, 8, 64, 512])
 def test_qwen3_parity(dev, T):
     """C4 shape (H=2048, I=768, E=128, top-8)."""
     from xcalibur_b200 import PreparedMoE

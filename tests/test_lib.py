@@ -45,8 +45,8 @@ def test_shape_checks():
 def test_packed_and_workspace_sizes():
     lib = _lib.load()
     s = _shape(E=256, H=7168, I=2048)
-    assert lib.xcb_moe_packed_bytes(ctypes.byref(s), 0) == 256 * 256 * 9 * 7168
-    assert lib.xcb_moe_packed_bytes(ctypes.byref(s), 1) == 256 * 448 * 9 * 2048
+    assert lib.xcb_moe_packed_bytes(ctypes.byref(s), 0) == 2 * 256 * 256 * 9 * 7168
+    assert lib.xcb_moe_packed_bytes(ctypes.byref(s), 1) == 2 * 256 * 448 * 9 * 2048
     n1 = lib.xcb_moe_workspace_bytes(ctypes.byref(s), 1, 8)
     n2 = lib.xcb_moe_workspace_bytes(ctypes.byref(s), 64, 8)
     assert 0 < n1 < n2

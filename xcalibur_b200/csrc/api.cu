@@ -23,6 +23,7 @@ int shape_ok(const XcbMoeShape* s) {
   if (s->hidden % 256 || s->inter % 256) return XCB_ERR_UNSUPPORTED;
   if (s->total_experts > 512 || s->num_experts > 512) return XCB_ERR_UNSUPPORTED;
   if (skinny_smem_bytes(s->hidden, s->inter) > 227 * 1024) return XCB_ERR_UNSUPPORTED;
+  if (wide_smem_bytes() > 227 * 1024) return XCB_ERR_UNSUPPORTED;
   return XCB_OK;
 }
 }  // namespace
@@ -46,7 +47,8 @@ int xcb_moe_check_shape(const XcbMoeShape* shape) { return shape_ok(shape); }
 size_t xcb_moe_packed_bytes(const XcbMoeShape* s, int which) {
   if (shape_ok(s) != XCB_OK) return 0;
   const size_t E = (size_t)s->num_experts, H = (size_t)s->hidden, I = (size_t)s->inter;
-  return which == 0 ? E * (2 * I / 16) * 9 * H : E * (H / 16) * 9 * I;
+  // decode-path layout followed by the prefill-path layout, equal sizes
+  return 2 * (which == 0 ? E * (2 * I / 16) * 9 * H : E * (H / 16) * 9 * I);
 }
 
 int xcb_moe_pack_weights(const XcbMoeShape* s, const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* w2,
@@ -89,10 +91,22 @@ int xcb_moe_workspace_init(void* ws, size_t bytes, int32_t max_tokens, int32_t t
 }
 
 namespace {
-// Validate a forward call and carve its workspace; shared by route / experts / forward.
-int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t ws_bytes, RouteParams* rp,
-                 SkinnyParams* sp) {
+// Routes per call from which xcb_moe_forward takes the prefill path (tensor-core grouped GEMMs) instead of the
+// decode kernel, unless a XCB_FLAG_*_PATH flag forces one.
+constexpr long long kPrefillMinRoutes = kSmallRoutes + 1;
+
+struct CallPlan {
+  RouteParams rp;
+  SkinnyParams sp;
+  WidePathParams wp;
+  bool wide;
+};
+
+// Validate a forward call, pick its path and carve its workspace; shared by route / experts / forward.
+int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t ws_bytes, CallPlan* plan) {
   if (!w || !a || !ws) return XCB_ERR_INVALID_ARG;
+  RouteParams* rp = &plan->rp;
+  SkinnyParams* sp = &plan->sp;
   const XcbMoeShape* s = &w->shape;
   int rc = shape_ok(s);
   if (rc != XCB_OK) return rc;
@@ -105,13 +119,17 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   if (have_logits == have_ids) return XCB_ERR_INVALID_ARG;
   const bool post_norm = (a->flags & XCB_FLAG_POST_NORM) != 0;
   if (post_norm && !w->post_norm_w) return XCB_ERR_INVALID_ARG;
-  if (a->flags & ~XCB_FLAG_POST_NORM) return XCB_ERR_INVALID_ARG;
+  if (a->flags & ~(XCB_FLAG_POST_NORM | XCB_FLAG_DECODE_PATH | XCB_FLAG_PREFILL_PATH)) return XCB_ERR_INVALID_ARG;
+  if ((a->flags & XCB_FLAG_DECODE_PATH) && (a->flags & XCB_FLAG_PREFILL_PATH)) return XCB_ERR_INVALID_ARG;
   if (!aligned16(a->hidden_states) || !aligned16(a->out) || !aligned16(w->gate_up) || !aligned16(w->down) ||
       !aligned16(ws))
     return XCB_ERR_INVALID_ARG;
   const WsLayout L = ws_layout(s->num_experts, s->hidden, s->inter, a->tokens, a->top_k);
   if (ws_bytes < L.total) return XCB_ERR_WORKSPACE;
   uint8_t* b = (uint8_t*)ws;
+  const long long routes = (long long)a->tokens * a->top_k;
+  plan->wide = (a->flags & XCB_FLAG_PREFILL_PATH) ||
+               (!(a->flags & XCB_FLAG_DECODE_PATH) && (routes >= kPrefillMinRoutes || a->tokens > kSmallTokens));
 
   rp->logits = a->router_logits;
   rp->ids_in = a->topk_ids;
@@ -131,10 +149,11 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   rp->jobs = (int4*)(b + L.jobs);
   rp->doneA = (int*)(b + L.doneA);
   rp->ss = (float*)(b + L.ss);
+  rp->hist = (int*)(b + L.hist);
   rp->ids_out = a->topk_ids_out;
   rp->wts_out = a->topk_weights_out;
 
-  const bool small = (size_t)a->tokens * a->top_k <= (size_t)kSmallRoutes && a->tokens <= kSmallTokens;
+  const bool small = !plan->wide && routes <= (long long)kSmallRoutes && a->tokens <= kSmallTokens;
   int* ctl = rp->ctl;
   *sp = SkinnyParams{};
   sp->wA = (const uint8_t*)w->gate_up;
@@ -181,37 +200,65 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   sp->post_norm = post_norm ? 1 : 0;
   sp->grid_combine = (post_norm || !small) ? 1 : 0;
   sp->timeout_ns = kTimeoutNs;
+
+  WidePathParams* wp = &plan->wp;
+  *wp = WidePathParams{};
+  const size_t E = (size_t)s->num_experts, H = (size_t)s->hidden, I = (size_t)s->inter;
+  wp->x = a->hidden_states;
+  wp->order = rp->order;
+  wp->pos = rp->pos;
+  wp->wts = rp->wts;
+  wp->offsets = rp->offsets;
+  wp->ctl = ctl;
+  wp->wA = (const uint8_t*)w->gate_up + E * (2 * I / 16) * 9 * H;  // prefill layout after the decode layout
+  wp->wB = (const uint8_t*)w->down + E * (H / 16) * 9 * I;
+  wp->gsA = w->gate_up_gs;
+  wp->gsB = w->down_gs;
+  wp->normw = w->post_norm_w;
+  wp->xperm = (uint16_t*)(b + L.y);  // gathered rows live in the y region: read by the gate_up GEMM before y is written
+  wp->inter = sp->inter;
+  wp->y = sp->y;
+  wp->ss = rp->ss;
+  wp->out = a->out;
+  wp->T = a->tokens;
+  wp->k = a->top_k;
+  wp->H = s->hidden;
+  wp->I = s->inter;
+  wp->E_loc = s->num_experts;
+  wp->post_norm = post_norm ? 1 : 0;
+  wp->timeout_ns = kTimeoutNs;
   return XCB_OK;
+}
+
+int run_experts(const CallPlan& plan, cudaStream_t stream) {
+  return plan.wide ? launch_wide_path(plan.wp, stream) : launch_skinny(plan.sp, stream);
 }
 }  // namespace
 
 int xcb_moe_route(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t ws_bytes, cudaStream_t stream) {
-  RouteParams rp;
-  SkinnyParams sp;
-  int rc = prepare_call(w, a, ws, ws_bytes, &rp, &sp);
+  CallPlan plan;
+  int rc = prepare_call(w, a, ws, ws_bytes, &plan);
   if (rc != XCB_OK || a->tokens == 0) return rc;
-  if (sp.small_route) return XCB_OK;  // small batches are routed inside the experts kernel
-  return launch_route(rp, stream);
+  if (plan.sp.small_route) return XCB_OK;  // small batches are routed inside the experts kernel
+  return launch_route(plan.rp, stream);
 }
 
 int xcb_moe_experts(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t ws_bytes, cudaStream_t stream) {
-  RouteParams rp;
-  SkinnyParams sp;
-  int rc = prepare_call(w, a, ws, ws_bytes, &rp, &sp);
+  CallPlan plan;
+  int rc = prepare_call(w, a, ws, ws_bytes, &plan);
   if (rc != XCB_OK || a->tokens == 0) return rc;
-  return launch_skinny(sp, stream);
+  return run_experts(plan, stream);
 }
 
 int xcb_moe_forward(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t ws_bytes, cudaStream_t stream) {
-  RouteParams rp;
-  SkinnyParams sp;
-  int rc = prepare_call(w, a, ws, ws_bytes, &rp, &sp);
+  CallPlan plan;
+  int rc = prepare_call(w, a, ws, ws_bytes, &plan);
   if (rc != XCB_OK || a->tokens == 0) return rc;
-  if (!sp.small_route) {
-    rc = launch_route(rp, stream);
+  if (!plan.sp.small_route) {
+    rc = launch_route(plan.rp, stream);
     if (rc != XCB_OK) return rc;
   }
-  return launch_skinny(sp, stream);
+  return run_experts(plan, stream);
 }
 
 // ------------------------------------------------------------------------------------------------ allocation-free

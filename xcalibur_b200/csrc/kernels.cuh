@@ -28,6 +28,7 @@ struct RouteParams {
   int4* jobs;
   int* doneA;              // per-job phase-A counters, zeroed here for the kernel that follows
   float* ss;
+  int* hist;               // [chunks][E_loc] per-chunk expert histograms, then chunk bases (many-token router)
   int* ids_out;
   float* wts_out;
 };
@@ -91,7 +92,46 @@ struct QuantParams {
   float* amax;
 };
 
+// One prefill-path GEMM (wide_kernel): mode 0 = gate_up + SwiGLU -> inter, mode 1 = down -> y.
+struct WideParams {
+  const uint8_t* w;        // prefill-layout packed weights of this GEMM
+  const float* gs;         // per-expert global scale
+  const int* offsets;      // [E_loc + 1] first permuted route of each expert
+  const uint16_t* normw;   // bf16 [H] (post-norm) or null
+  uint16_t* inter;         // mode 0 output, bf16 [routes, I]
+  float* y;                // mode 1 output, fp32 [routes, H]
+  float* ss;               // mode 1 post-norm sums of squares [routes]
+  int* status;
+  int E_loc, R, K, I, H;
+  int mode, post_norm;
+  unsigned long long timeout_ns;
+};
+
+// The whole prefill path after the router: gather, gate_up GEMM, down GEMM, combine.
+struct WidePathParams {
+  const uint16_t* x;
+  const int* order;
+  const int* pos;
+  const float* wts;
+  const int* offsets;
+  int* ctl;
+  const uint8_t* wA;       // prefill-layout regions of the packed buffers
+  const uint8_t* wB;
+  const float* gsA;
+  const float* gsB;
+  const uint16_t* normw;
+  uint16_t* xperm;
+  uint16_t* inter;
+  float* y;
+  float* ss;
+  uint16_t* out;
+  int T, k, H, I, E_loc, post_norm;
+  unsigned long long timeout_ns;
+};
+
 int launch_route(const RouteParams& p, cudaStream_t stream);
+int launch_wide_path(const WidePathParams& p, cudaStream_t stream);
+size_t wide_smem_bytes();
 size_t route_smem_bytes(int E_loc);
 int launch_skinny(const SkinnyParams& p, cudaStream_t stream);
 size_t skinny_smem_bytes(int H, int I);

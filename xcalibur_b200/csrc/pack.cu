@@ -90,10 +90,70 @@ __global__ void pack_scales_kernel(PackParams p) {
   }
 }
 
+// ------------------------------------------------------------------------------------------------ prefill layout
+// Original row of wide-layout packed row pr: per 128-row block, lanes 0-31 gate / 32-63 up / 64-95 gate / 96-127 up
+// of the block's 64 features (gate_up); identity for down.
+__device__ __forceinline__ int wide_orig_row(int pr, int R, int gate_up) {
+  if (!gate_up) return pr;
+  const int b = pr >> 7, q = (pr >> 5) & 3, i = pr & 31;
+  return 64 * b + 32 * (q >> 1) + i + ((q & 1) ? (R >> 1) : 0);
+}
+
+// One thread per packed word: the row's 4 code bytes at k/2 (k = 8 consecutive weights of one row), folded by the
+// block's scale and sent through T.
+__global__ void pack_wide_codes_kernel(PackParams p) {
+  __shared__ uint32_t tab[4][256];
+  for (int i = threadIdx.x; i < 1024; i += blockDim.x) tab[i >> 8][i & 255] = p.tabs[i];
+  __syncthreads();
+  const int ns = p.K / 256, nb = p.R / 128;
+  const size_t total = (size_t)p.E * p.R * (p.K / 8);
+  const size_t K2 = p.K / 2, K16 = p.K / 16;
+  for (size_t w = (size_t)blockIdx.x * blockDim.x + threadIdx.x; w < total; w += (size_t)gridDim.x * blockDim.x) {
+    const int wq = (int)(w & 3), row = (int)((w >> 2) & 127), j = (int)((w >> 9) & 1), c = (int)((w >> 10) & 3);
+    const size_t rest = w >> 12;
+    const int s = (int)(rest % ns);
+    const size_t ub = rest / ns;  // e * nb + b
+    const int b = (int)(ub % nb), e = (int)(ub / nb);
+    const int ro = wide_orig_row(128 * b + row, p.R, p.gate_up);
+    const int k = 256 * s + 64 * c + 32 * j + 8 * wq;
+    const size_t rbase = (size_t)e * p.R + ro;
+    int f;
+    scale_code(p.sf[rbase * K16 + k / 16], f);
+    if (f == 3) set_status(p.status, XCB_STATUS_NAN_SCALE);
+    uint32_t word = *reinterpret_cast<const uint32_t*>(p.codes + rbase * K2 + k / 2);
+    word = f == 1 ? 0u : (f == 2 ? word ^ 0x88888888u : word);
+    const uint32_t packed = tab[0][word & 255] ^ tab[1][(word >> 8) & 255] ^ tab[2][(word >> 16) & 255] ^ tab[3][word >> 24];
+    reinterpret_cast<uint32_t*>(p.out + ((ub * ns + s) * 4 + c) * 4608)[(j * 128 + row) * 4 + wq] = packed;
+  }
+}
+
+__global__ void pack_wide_scales_kernel(PackParams p) {
+  const int ns = p.K / 256, nb = p.R / 128;
+  const size_t total = (size_t)p.E * p.R * (p.K / 16);
+  const size_t K16 = p.K / 16;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int blk = (int)(i & 3), row = (int)((i >> 2) & 127), c = (int)((i >> 9) & 3);
+    const size_t rest = i >> 11;
+    const int s = (int)(rest % ns);
+    const size_t ub = rest / ns;
+    const int b = (int)(ub % nb), e = (int)(ub / nb);
+    const int ro = wide_orig_row(128 * b + row, p.R, p.gate_up);
+    int f;
+    const uint32_t code = scale_code(p.sf[((size_t)e * p.R + ro) * K16 + 16 * s + 4 * c + blk], f);
+    p.out[((ub * ns + s) * 4 + c) * 4608 + 4096 + row * 4 + blk] = (uint8_t)code;
+  }
+}
+
 int launch_pack(const PackParams& p, cudaStream_t stream) {
   pack_codes_kernel<<<148 * 8, 256, 0, stream>>>(p);
   if (cudaGetLastError() != cudaSuccess) return XCB_ERR_CUDA;
   pack_scales_kernel<<<148 * 4, 256, 0, stream>>>(p);
+  if (cudaGetLastError() != cudaSuccess) return XCB_ERR_CUDA;
+  PackParams q = p;
+  q.out = p.out + (size_t)p.E * (p.R / 16) * 9 * (size_t)p.K;  // the prefill layout follows the decode layout
+  pack_wide_codes_kernel<<<148 * 8, 256, 0, stream>>>(q);
+  if (cudaGetLastError() != cudaSuccess) return XCB_ERR_CUDA;
+  pack_wide_scales_kernel<<<148 * 4, 256, 0, stream>>>(q);
   return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
 }
 

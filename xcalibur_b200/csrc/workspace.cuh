@@ -4,6 +4,7 @@
 // before it is read (the router zeroes the per-job counters), so consecutive calls of any size on one stream
 // need no host-side reset and stay graph-capturable.
 #pragma once
+#include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
 
@@ -26,8 +27,15 @@ enum CtlWord : int {
 constexpr int kSmallRoutes = 256;  // T*k up to which the decode kernel routes in-kernel (one launch per call)
 constexpr int kSmallTokens = 32;
 
+// The many-token router works on chunks of whole tokens, at most 1024 routes each.
+__host__ __device__ inline int route_chunk_tokens(int top_k) { return top_k > 0 && top_k <= 1024 ? 1024 / top_k : 1; }
+__host__ __device__ inline size_t route_chunks(int tokens, int top_k) {
+  const int ct = route_chunk_tokens(top_k);
+  return ((size_t)tokens + ct - 1) / ct;
+}
+
 struct WsLayout {
-  size_t ctl, ids, wts, pos, order, counts, offsets, jobs, doneA, ss, inter, y, total;
+  size_t ctl, ids, wts, pos, order, counts, offsets, jobs, doneA, ss, hist, inter, y, total;
   int max_routes, max_jobs;
 };
 
@@ -55,6 +63,7 @@ inline WsLayout ws_layout(int E_loc, int H, int I, int max_tokens, int top_k) {
   L.jobs = take((size_t)L.max_jobs * 16);
   L.doneA = take((size_t)L.max_jobs * 4);
   L.ss = take(R * 4);
+  L.hist = take(route_chunks(max_tokens, top_k) * (size_t)E_loc * 4);
   L.inter = take(R * (size_t)I * 2);
   L.y = take(R * (size_t)H * 4);
   L.total = o;

@@ -86,6 +86,9 @@ def _xor_tables(device: torch.device) -> torch.Tensor:
     return _TABLES[key]
 
 
+_PATH_FLAGS = {"auto": 0, "decode": _lib.XCB_FLAG_DECODE_PATH, "prefill": _lib.XCB_FLAG_PREFILL_PATH}
+
+
 class PreparedMoE:
     """Packed weights of one MoE layer on one GPU plus its per-stream workspaces.
 
@@ -154,8 +157,12 @@ class PreparedMoE:
     # -------------------------------------------------------------------------------------- forward
     def build_call(self, hidden_states: torch.Tensor, router_logits: Optional[torch.Tensor] = None, top_k: int = 8,
                    *, topk_ids: Optional[torch.Tensor] = None, topk_weights: Optional[torch.Tensor] = None,
-                   post_norm: bool = False, out: Optional[torch.Tensor] = None, return_routing: bool = False):
-        """Validate one call and bind its buffers; returns a ``LayerCall`` whose ``launch()`` enqueues it."""
+                   post_norm: bool = False, out: Optional[torch.Tensor] = None, return_routing: bool = False,
+                   path: str = "auto"):
+        """Validate one call and bind its buffers; returns a ``LayerCall`` whose ``launch()`` enqueues it.
+
+        ``path``: "auto" (the library picks by batch size), "decode" (the streaming decode kernel) or "prefill"
+        (the tensor-core grouped GEMMs)."""
         x = hidden_states
         if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != self.H:
             raise ValueError(f"hidden_states must be bf16 [T, {self.H}]")
@@ -187,15 +194,19 @@ class PreparedMoE:
             ids_out = torch.empty((T, top_k), dtype=torch.int32, device=self.device)
             wts_out = torch.empty((T, top_k), dtype=torch.float32, device=self.device)
         ws = self.workspace(T, top_k) if T else None
-        args = XcbMoeArgs(T, top_k, _lib.XCB_FLAG_POST_NORM if post_norm else 0, 0, x.data_ptr(), _ptr(logits),
+        if path not in _PATH_FLAGS:
+            raise ValueError(f"path must be one of {sorted(_PATH_FLAGS)}")
+        flags = (_lib.XCB_FLAG_POST_NORM if post_norm else 0) | _PATH_FLAGS[path]
+        args = XcbMoeArgs(T, top_k, flags, 0, x.data_ptr(), _ptr(logits),
                           _ptr(ids), _ptr(wts), out.data_ptr(), _ptr(ids_out), _ptr(wts_out))
         return LayerCall(self, args, ws, (x, logits, ids, wts), out, ids_out, wts_out, return_routing)
 
     def forward(self, hidden_states: torch.Tensor, router_logits: Optional[torch.Tensor] = None, top_k: int = 8, *,
                 topk_ids: Optional[torch.Tensor] = None, topk_weights: Optional[torch.Tensor] = None,
-                post_norm: bool = False, out: Optional[torch.Tensor] = None, return_routing: bool = False):
+                post_norm: bool = False, out: Optional[torch.Tensor] = None, return_routing: bool = False,
+                path: str = "auto"):
         call = self.build_call(hidden_states, router_logits, top_k, topk_ids=topk_ids, topk_weights=topk_weights,
-                               post_norm=post_norm, out=out, return_routing=return_routing)
+                               post_norm=post_norm, out=out, return_routing=return_routing, path=path)
         call.launch()
         return call.result()
 

@@ -32,6 +32,20 @@ Decode-path ("skinny") layout of one expert matrix W [R rows, K] (K % 256 == 0, 
   ``2^E (1 + m/8)``, E in [-9, 8] (the E4M3 subnormals become normal).  The kernel forms the bf16 factor
   ``(c << 4) | 0x6000`` = value * 2^74 with one integer multiply-add; the decoded weight in bf16 is
   exactly ``e2m1 * sf * 2^-52`` and the epilogue multiplies by ``gs * 2^52``.
+
+Prefill-path ("wide") layout of the same matrix, stored after the decode-path bytes in the same buffer.  It feeds
+the tcgen05 kernel, whose dequantising threads write one weight row each into a tensor-memory lane (the MMA's A
+operand), so a word holds 8 consecutive k of ONE row:
+
+* Rows are cut into blocks of 128 packed rows (one per TMEM lane).  For gate_up, block ``b`` holds lanes 0-31 =
+  gate rows 64b..64b+31, 32-63 = the up rows of the same features, 64-95 = gate 64b+32..64b+63, 96-127 = their up
+  rows; down keeps rows in order.
+* A block is ``K/256`` stages of 18432 bytes (256 k each); a stage is 4 chunks of 4608 bytes (64 k); a chunk is
+  its codes ``[2 halves][128 rows][4 words]`` u32 (4096 bytes; half j, word w cover k = 64c + 32j + 8w .. +7) then
+  its scale codes ``[128 rows][4 blocks]`` bytes (512).  The blocks of one expert are consecutive.
+* The natural word is the row's 4 code bytes at k/2 (low nibble = even k), so the decoder's register i holds
+  (k + 2i, k + 2i + 1), exactly a tensor-memory column of two bf16; it is stored as ``T(word)`` with the same T
+  and the same scale canonicalisation as the decode-path layout.
 """
 from __future__ import annotations
 
@@ -174,6 +188,21 @@ def group_slices(K: int) -> int:
 
 def unit_bytes(K: int) -> int:
     return 9 * K
+
+
+WIDE_ROWS = 128          # rows per wide-layout block (tensor-memory lanes)
+WIDE_STAGE_BYTES = 18432 # 256 k x 128 rows
+WIDE_CHUNK_BYTES = 4608  # 64 k x 128 rows
+
+
+def wide_bytes(E: int, R: int, K: int) -> int:
+    """Packed bytes of one [E, R, K] tensor in the prefill-path layout (same as the decode-path size)."""
+    return E * (R // WIDE_ROWS) * (K // 256) * WIDE_STAGE_BYTES
+
+
+def packed_bytes(E: int, R: int, K: int) -> int:
+    """Bytes of one packed tensor buffer: the decode-path layout followed by the prefill-path layout."""
+    return skinny_bytes(E, R, K) + wide_bytes(E, R, K)
 
 
 def skinny_bytes(E: int, R: int, K: int) -> int:

@@ -46,7 +46,11 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gib", type=float, default=4.0)
     ap.add_argument("--windows", default="", help="comma-separated MiB per launch (rotating offsets), e.g. 66,132,512")
+    ap.add_argument("--l2-mb", type=int, default=0,
+                    help="L2 read bandwidth instead: every CTA streams the same L2-resident block of this many MiB")
     a = ap.parse_args()
+    if a.l2_mb:
+        return l2_sweep(a.l2_mb)
     buf = torch.empty(int(a.gib * (1 << 30)), dtype=torch.uint8, device="cuda")
     buf.random_(0, 255)
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
@@ -72,6 +76,36 @@ def main():
                                   "chunk": chunk, "stages": stages, "ctas_per_sm": ctas, "threads": threads,
                                   "window_mb": window >> 20, "regions": nreg, "gbs": round(gbs, 1),
                                   "status": int(status.item())}), flush=True)
+
+
+def l2_sweep(mb: int):
+    """Every CTA reads the same ``mb`` MiB (regions all at offset 0), so after the first pass the stream is served
+    by L2: the figure bounds how fast a kernel can refill shared memory from L2-resident operands."""
+    lib = _lib.load()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    per = mb << 20
+    buf = torch.empty(per + (1 << 20), dtype=torch.uint8, device="cuda")
+    buf.random_(0, 255)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sink = torch.zeros(1, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for chunk, stages, ctas, threads in ((16384, 8, 1, 128), (32768, 6, 1, 128), (16384, 6, 2, 128),
+                                         (4096, 16, 1, 128)):
+        G = sms * ctas
+        regions = torch.zeros(G, dtype=torch.int64, device="cuda")
+        total = per * G
+        best = None
+        for r in range(4):
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            _lib.check(lib.xcb_hbm_probe(buf.data_ptr(), total, 0, chunk, stages, ctas, threads, regions.data_ptr(), G,
+                                         status.data_ptr(), sink.data_ptr(), stream), "xcb_hbm_probe")
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        print(json.dumps({"mode": "l2_bulk_ring", "block_mb": mb, "chunk": chunk, "stages": stages, "ctas_per_sm": ctas,
+                          "gbs": round(total / (best * 1e-3) / 1e9, 1), "status": int(status.item())}), flush=True)
 
 
 if __name__ == "__main__":
