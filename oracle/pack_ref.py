@@ -1,8 +1,8 @@
-"""CPU model of the decode-path weight layout — test infrastructure.
+"""CPU model of both packed weight layouts — test infrastructure.
 
-Builds, with numpy, the exact bytes the GPU packer (``xcb_moe_pack_weights``) must produce, from the layout and
-bit map that ``xcalibur_b200.packer`` defines, and decodes packed bytes back to weight values the way the
-kernel's registers see them.  The reference analogue is the host repack of
+Builds, with numpy, the exact bytes the GPU packer (``xcb_moe_pack_weights``) must produce, from the layouts and
+bit maps that ``xcalibur_b200.packer`` defines, and decodes packed bytes back to weight values the way the
+kernels' registers see them.  The reference analogue is the host repack of
 kernels/moe_w4a16_h200/moe_w4a16.py:3168-3190 plus its GF(2) word transform at :3903-3933.
 """
 from __future__ import annotations
@@ -41,7 +41,8 @@ SCALE_CODE, SCALE_FOLD = _scale_tables()
 
 
 def canonical(codes: np.ndarray, sf: np.ndarray):
-    """Fold zero and negative scales into the codes; return (codes', scale codes) for one [R, K/2] matrix."""
+    """Fold zero and negative scales into the codes; return (codes', scale codes) for one [R, K/2] matrix
+    (prefill-path layout only)."""
     R, K2 = codes.shape
     fold = SCALE_FOLD[sf]                                        # [R, K/16]
     fold_b = np.repeat(fold, 8, axis=1)[:, :K2]                  # per code byte (8 bytes per 16-k block)
@@ -58,42 +59,19 @@ def _apply_T(words: np.ndarray) -> np.ndarray:
     return (tabs[0][w & 255] ^ tabs[1][(w >> 8) & 255] ^ tabs[2][(w >> 16) & 255] ^ tabs[3][w >> 24]).astype(np.uint32)
 
 
-def join_units(code_bytes: np.ndarray, scale_bytes: np.ndarray) -> np.ndarray:
-    """[nb, nS*512] codes + [nb, nS*64] scales -> [nb, 9K] units: per group of gs slices, its codes then its scales."""
-    nb = code_bytes.shape[0]
-    nS = code_bytes.shape[1] // 512
-    gs = packer.group_slices(64 * nS)
-    parts = []
-    for g0 in range(0, nS, gs):
-        ns = gs
-        parts.append(code_bytes[:, g0 * 512:(g0 + ns) * 512])
-        parts.append(scale_bytes[:, g0 * 64:(g0 + ns) * 64])
-    return np.concatenate(parts, axis=1).reshape(nb, -1)
-
-
-def split_units(units: np.ndarray, K: int):
-    """Inverse of join_units: [nb, 9K] -> ([nb, nS*512] codes, [nb, nS*64] scales)."""
-    nS = K // 64
-    gs = packer.group_slices(K)
-    cs, ss = [], []
-    off = 0
-    for g0 in range(0, nS, gs):
-        ns = gs
-        cs.append(units[:, off:off + ns * 512])
-        ss.append(units[:, off + ns * 512:off + ns * 576])
-        off += ns * 576
-    return np.concatenate(cs, axis=1), np.concatenate(ss, axis=1)
-
-
 def pack_matrix(codes: np.ndarray, sf: np.ndarray, gate_up: bool) -> np.ndarray:
-    """One expert matrix (codes [R, K/2], sf [R, K/16]) -> packed bytes [R/16 units, 9K]."""
+    """One expert matrix (codes [R, K/2], sf [R, K/16]) -> decode-path packed bytes [R/16 units, 9K].
+
+    A unit is K/64 slice records of 576 bytes: ``[32 lanes][4 words]`` of codes, then ``[32 lanes][2]`` scale bytes.
+    Word j of lane 4g + t in slice S = raw code bytes (row g, row g + 8, row g, row g + 8) at code byte
+    32S + 8t + 2j + (0, 0, 1, 1); the lane's two scale bytes are the raw E4M3 scales of rows g and g + 8 for
+    block 4S + t."""
     R, K2 = codes.shape
     K = 2 * K2
     rows = packed_row_order(R, gate_up)
-    c, sc = canonical(codes[rows], sf[rows])
+    c, sc = codes[rows], sf[rows]
     nb, nS = R // 16, K // 64
     cb = c.reshape(nb, 2, 8, K2)                                 # [rb, h, g, byte]
-    # byte index for (S, t, j, hi): 32S + 8t + 2j + hi
     S = np.arange(nS)[:, None, None, None]
     t = np.arange(4)[None, :, None, None]
     j = np.arange(4)[None, None, :, None]
@@ -103,19 +81,16 @@ def pack_matrix(codes: np.ndarray, sf: np.ndarray, gate_up: bool) -> np.ndarray:
     r8 = cb[:, 1][:, :, bidx]                                    # rows g + 8
     word = (r0[..., 0].astype(np.uint32) | (r8[..., 0].astype(np.uint32) << 8)
             | (r0[..., 1].astype(np.uint32) << 16) | (r8[..., 1].astype(np.uint32) << 24))  # [rb, g, S, t, j]
-    word = _apply_T(word)
     word = word.transpose(0, 2, 1, 3, 4)                         # [rb, S, g, t, j] -> lane = 4g + t
-    code_bytes = np.ascontiguousarray(word).view(np.uint8).reshape(nb, nS * 512)
+    code_bytes = np.ascontiguousarray(word).view(np.uint8).reshape(nb, nS, 512)
     sb = sc.reshape(nb, 2, 8, K // 16)                           # [rb, h, g, block]
-    S4 = np.arange(nS // 4)[:, None, None, None, None]
-    g = np.arange(8)[None, :, None, None, None]
-    tt = np.arange(4)[None, None, :, None, None]
-    s4 = np.arange(4)[None, None, None, :, None]
-    h = np.arange(2)[None, None, None, None, :]
-    blk = 4 * (4 * S4 + s4) + tt                                 # scale block of (slice, t)
-    scl = sb[:, h, g, blk]                                        # [rb, S4, g, t, s4, h]
-    scale_bytes = np.ascontiguousarray(scl).reshape(nb, K)
-    return join_units(code_bytes, scale_bytes)
+    g = np.arange(8)[None, :, None, None]
+    tt = np.arange(4)[None, None, :, None]
+    S2 = np.arange(nS)[:, None, None, None]
+    h = np.arange(2)[None, None, None, :]
+    scl = sb[:, h, g, 4 * S2 + tt]                               # [rb, S, g, t, h]
+    scale_bytes = np.ascontiguousarray(scl).reshape(nb, nS, 64)
+    return np.concatenate([code_bytes, scale_bytes], axis=2).reshape(nb, 9 * K)
 
 
 def pack_tensor(codes: np.ndarray, sf: np.ndarray, gate_up: bool) -> np.ndarray:
@@ -124,38 +99,28 @@ def pack_tensor(codes: np.ndarray, sf: np.ndarray, gate_up: bool) -> np.ndarray:
 
 
 def unpack_matrix_values(units: np.ndarray, R: int, K: int, gate_up: bool) -> np.ndarray:
-    """Decode packed units back to fp32 weights (without gs) in the ORIGINAL row order, the kernel's way:
-    run D on every word, read each bf16 field (value e2m1 * 2^-126), multiply by the scale code's value."""
+    """Decode packed units back to fp32 weights (without gs) in the ORIGINAL row order, the way the kernel's
+    registers see them: each code byte -> two E2M1 values (low nibble first), times the lane's E4M3 scale."""
     nb, nS = R // 16, K // 64
-    code_bytes, scale_bytes = split_units(units, K)
-    words = np.ascontiguousarray(code_bytes).view(np.uint32).reshape(nb, nS, 8, 4, 4)   # rb, S, g, t, j
-    M = packer.FIELD_MASK
-    q = words.astype(np.uint64)
-    rotl = lambda v, s: ((v << s) | (v >> (32 - s))) & 0xFFFFFFFF
-    u6 = (q << 6) & 0xFFFFFFFF
-    regs = [q & M, (q << 4) & M, (u6 ^ rotl(q, 10)) & M, (u6 ^ rotl(q, 12)) & M]
+    rec = np.ascontiguousarray(units).reshape(nb, nS, 576)
+    words = rec[:, :, :512].copy().view(np.uint32).reshape(nb, nS, 8, 4, 4)          # rb, S, g, t, j
+    scl = rec[:, :, 512:].reshape(nb, nS, 8, 4, 2)                                  # rb, S, g, t, h
+    sval = nvfp4.e4m3_decode(scl)
     out = np.zeros((nb, 16, K), dtype=np.float32)
-    sb = np.ascontiguousarray(scale_bytes).reshape(nb, nS // 4, 8, 4, 4, 2)          # rb, S4, g, t, s4, h
-    for i, r in enumerate(regs):
-        for hh in range(2):
-            bits = ((r >> (16 * hh)) & 0xFFFF).astype(np.uint32) << 16
-            val = (bits.astype(np.uint32)).view(np.float32) * np.float32(2.0 ** 126)   # e2m1 value
-            row_h = i & 1                 # registers 0, 2 -> row g; 1, 3 -> row g + 8
-            koff = 2 * (i >> 1) + hh      # registers 0, 1 -> k+0/+1; 2, 3 -> k+2/+3
-            S = np.arange(nS)[:, None, None, None]
-            t = np.arange(4)[None, None, :, None]
-            j = np.arange(4)[None, None, None, :]
-            k = 64 * S + 16 * t + 4 * j + koff                                     # [S, 1, t, j]
-            g = np.arange(8)[None, :, None, None]
-            sc = sb[:, :, :, :, :, row_h]                                           # rb, S4, g, t, s4
-            scode = sc.reshape(nb, nS // 4, 8, 4, 4).transpose(0, 1, 4, 2, 3).reshape(nb, nS, 8, 4)  # rb,S,g,t
-            sval = np.vectorize(packer.scale_code_value)(scode).astype(np.float32)
-            w = val * sval[..., None]
-            rows = g + 8 * row_h
+    S = np.arange(nS)[:, None, None, None]
+    t = np.arange(4)[None, None, :, None]
+    j = np.arange(4)[None, None, None, :]
+    g = np.arange(8)[None, :, None, None]
+    for b in range(4):                           # byte b of the word: register b of the step
+        byte = (words >> (8 * b)) & 0xFF
+        row_h = b & 1                            # bytes 0, 2 -> row g; 1, 3 -> row g + 8
+        for nib in range(2):                     # low nibble -> even k
+            val = nvfp4.E2M1_VALUES[(byte >> (4 * nib)) & 0xF] * sval[..., row_h][..., None]
+            k = 64 * S + 16 * t + 4 * j + 2 * (b >> 1) + nib
             kk = np.broadcast_to(k, (nS, 8, 4, 4))
-            rr = np.broadcast_to(rows, (nS, 8, 4, 4))
-            for b in range(nb):
-                out[b, rr, kk] = w[b]
+            rr = np.broadcast_to(g + 8 * row_h, (nS, 8, 4, 4))
+            for u in range(nb):
+                out[u, rr, kk] = val[u]
     vals = out.reshape(R, K)
     orig = np.empty_like(vals)
     orig[packed_row_order(R, gate_up)] = vals

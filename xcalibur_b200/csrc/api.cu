@@ -22,7 +22,6 @@ int shape_ok(const XcbMoeShape* s) {
   if (s->expert_offset + s->num_experts > s->total_experts) return XCB_ERR_INVALID_ARG;
   if (s->hidden % 256 || s->inter % 256) return XCB_ERR_UNSUPPORTED;
   if (s->total_experts > 512 || s->num_experts > 512) return XCB_ERR_UNSUPPORTED;
-  if (skinny_smem_bytes(s->hidden, s->inter) > 227 * 1024) return XCB_ERR_UNSUPPORTED;
   if (wide_smem_bytes() > 227 * 1024) return XCB_ERR_UNSUPPORTED;
   return XCB_OK;
 }
@@ -130,6 +129,11 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   const long long routes = (long long)a->tokens * a->top_k;
   plan->wide = (a->flags & XCB_FLAG_PREFILL_PATH) ||
                (!(a->flags & XCB_FLAG_DECODE_PATH) && (routes >= kPrefillMinRoutes || a->tokens > kSmallTokens));
+  if (!plan->wide && !skinny_supported(s->hidden, s->inter)) {
+    // no stage plan of the decode kernel fits this shape: the tensor-core path serves every batch size
+    if (a->flags & XCB_FLAG_DECODE_PATH) return XCB_ERR_UNSUPPORTED;
+    plan->wide = true;
+  }
 
   rp->logits = a->router_logits;
   rp->ids_in = a->topk_ids;
@@ -196,6 +200,8 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
     // with precomputed ids one expert may repeat within a token, so a job can hold up to T*k tokens
     const long long per_job = have_logits ? a->tokens : (long long)a->tokens * a->top_k;
     sp->job_tokens = (int)(per_job < kJobTokens ? per_job : kJobTokens);
+    // the in-kernel router may split jobs finer, so that the shared-memory plan keeps its large stages
+    if (small) sp->job_tokens = skinny_job_cap(s->hidden, s->inter, sp->job_tokens, (int)routes);
   }
   sp->post_norm = post_norm ? 1 : 0;
   sp->grid_combine = (post_norm || !small) ? 1 : 0;

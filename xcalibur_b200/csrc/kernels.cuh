@@ -6,13 +6,6 @@
 
 namespace xcb {
 
-// Slices (64 k each) per group of the packed decode-path layout for a reduction length K (K % 256 == 0): the
-// largest of 16, 12, 8, 4 that divides K / 64, so every unit is a whole number of equal groups.
-__host__ __device__ inline int group_slices(int K) {
-  const int n = K / 64;
-  return n % 16 == 0 ? 16 : (n % 12 == 0 ? 12 : (n % 8 == 0 ? 8 : 4));
-}
-
 struct RouteParams {
   const float* logits;     // [T, E_tot] or null
   const int* ids_in;       // [T, k] or null
@@ -67,9 +60,9 @@ struct SkinnyParams {
   float* ss;              // fp32 [routes]
   uint16_t* out;          // bf16 [T, H]
   int T, k, H, I;
-  int job_tokens;         // most tokens one job can hold (sizes the activation staging)
+  int job_tokens;         // most tokens one job holds (sizes the activation staging; the in-kernel router's job split)
   int post_norm;
-  int grid_combine;       // 1: grid barrier + distributed combine; 0: per-row-block combine by the last unit
+  int grid_combine;       // 1: grid barrier + distributed combine; 0: per-row-block combine by the CTA completing it
   unsigned long long timeout_ns;
 };
 
@@ -134,7 +127,8 @@ int launch_wide_path(const WidePathParams& p, cudaStream_t stream);
 size_t wide_smem_bytes();
 size_t route_smem_bytes(int E_loc);
 int launch_skinny(const SkinnyParams& p, cudaStream_t stream);
-size_t skinny_smem_bytes(int H, int I);
+bool skinny_supported(int H, int I);  // the decode kernel has a stage plan for this shape
+int skinny_job_cap(int H, int I, int want, int route_R);
 int launch_pack(const PackParams& p, cudaStream_t stream);
 int launch_quantize(const QuantParams& p, cudaStream_t stream);
 

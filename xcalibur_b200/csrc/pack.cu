@@ -3,7 +3,9 @@
 // The packer replaces the reference's host-side torch repack (kernels/moe_w4a16_h200/moe_w4a16.py:3168-3190
 // _pack_codes/_pack_scales, GF(2) word transform :3903-3933), which takes ~0.8 s per 8192x4096 tensor on a CPU;
 // here one thread writes one packed word and the 6.3 GB of DeepSeek-V3-shaped weights pack in well under a
-// second.  Layout and bit map: xcalibur_b200/packer.py (module docstring).
+// second.  Two layouts per tensor: the decode-path layout (raw codes in m16n8k16 fragment order for the hardware
+// FP4 converter) and, after it, the prefill-path layout (GF(2)-transformed words for the tensor-memory kernel).
+// Layouts and bit map: xcalibur_b200/packer.py (module docstring).
 #include <cuda_fp8.h>
 
 #include "common.cuh"
@@ -30,18 +32,16 @@ __device__ __forceinline__ int orig_row(int pr, int R, int gate_up) {
   return r < 8 ? blk * 8 + r : (R >> 1) + blk * 8 + (r - 8);
 }
 
-__device__ __forceinline__ uint8_t fold_byte(uint8_t c, int fold) {
-  return fold == 1 ? (uint8_t)0 : (fold == 2 ? (uint8_t)(c ^ 0x88u) : c);
-}
-
+// Decode-path layout: per 16-row unit, K/64 slice records of 576 bytes, [32 lanes][4 words] of codes then
+// [32 lanes][2] scale bytes.  Word j of lane L = 4g + t in slice S holds the raw code bytes
+// (row g, row g + 8, row g, row g + 8) at code byte 32S + 8t + 2j, +0, +1, +1 (low nibble = even k): exactly the
+// f16x2 registers cvt.rn.f16x2.e2m1x2 produces for the four m16n8k16 A fragments.  The scale bytes of lane L are
+// the raw E4M3 scales of rows g and g + 8 for block 4S + t (cvt.rn.f16x2.e4m3x2 takes them as they are).
 __global__ void pack_codes_kernel(PackParams p) {
-  __shared__ uint32_t tab[4][256];
-  for (int i = threadIdx.x; i < 1024; i += blockDim.x) tab[i >> 8][i & 255] = p.tabs[i];
-  __syncthreads();
   const int nS = p.K / 64, nb = p.R / 16;
   const size_t words_per_unit = (size_t)nS * 128;
   const size_t total = (size_t)p.E * nb * words_per_unit;
-  const size_t K2 = p.K / 2, K16 = p.K / 16;
+  const size_t K2 = p.K / 2;
   for (size_t w = (size_t)blockIdx.x * blockDim.x + threadIdx.x; w < total; w += (size_t)gridDim.x * blockDim.x) {
     const int j = (int)(w & 3), lane = (int)((w >> 2) & 31);
     const size_t rest = w >> 7;
@@ -53,40 +53,30 @@ __global__ void pack_codes_kernel(PackParams p) {
     const size_t bidx = (size_t)32 * S + 8 * t + 2 * j;
     const uint8_t* c0 = p.codes + ((size_t)e * p.R + ro0) * K2;
     const uint8_t* c1 = p.codes + ((size_t)e * p.R + ro1) * K2;
-    const int blk = 4 * S + t;
-    int f0, f1;
-    scale_code(p.sf[((size_t)e * p.R + ro0) * K16 + blk], f0);
-    scale_code(p.sf[((size_t)e * p.R + ro1) * K16 + blk], f1);
-    if (f0 == 3 || f1 == 3) set_status(p.status, XCB_STATUS_NAN_SCALE);
-    const uint32_t word = (uint32_t)fold_byte(c0[bidx], f0) | ((uint32_t)fold_byte(c1[bidx], f1) << 8) |
-                          ((uint32_t)fold_byte(c0[bidx + 1], f0) << 16) | ((uint32_t)fold_byte(c1[bidx + 1], f1) << 24);
-    const uint32_t packed = tab[0][word & 255] ^ tab[1][(word >> 8) & 255] ^ tab[2][(word >> 16) & 255] ^ tab[3][word >> 24];
-    // unit = groups of gs slices, each group's codes followed by its scale codes
-    const int gs = group_slices(p.K), grp = S / gs, s = S % gs;
-    uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + ub * (size_t)9 * p.K + (size_t)grp * gs * 576) + s * 128 + lane * 4 + j;
-    *dst = packed;
+    const uint32_t word = (uint32_t)c0[bidx] | ((uint32_t)c1[bidx] << 8) | ((uint32_t)c0[bidx + 1] << 16) |
+                          ((uint32_t)c1[bidx + 1] << 24);
+    reinterpret_cast<uint32_t*>(p.out + ub * (size_t)9 * p.K + (size_t)S * 576)[lane * 4 + j] = word;
   }
 }
 
 __global__ void pack_scales_kernel(PackParams p) {
-  const int nb = p.R / 16, nS4 = p.K / 256;
-  const size_t per_unit = (size_t)p.K;  // scale bytes per unit
-  const size_t total = (size_t)p.E * nb * per_unit;
+  const int nS = p.K / 64, nb = p.R / 16;
+  const size_t total = (size_t)p.E * nb * nS * 32;  // one thread per (unit, slice, lane): two bytes
   const size_t K16 = p.K / 16;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    const int h = (int)(i & 1), s4 = (int)((i >> 1) & 3), lane = (int)((i >> 3) & 31);
-    const size_t rest = i >> 8;
-    const int S4 = (int)(rest % nS4);
-    const size_t ub = rest / nS4;
+    const int lane = (int)(i & 31);
+    const size_t rest = i >> 5;
+    const int S = (int)(rest % nS);
+    const size_t ub = rest / nS;
     const int rb = (int)(ub % nb), e = (int)(ub / nb);
     const int g = lane >> 2, t = lane & 3;
-    const int ro = orig_row(rb * 16 + g + 8 * h, p.R, p.gate_up);
-    const int blk = 4 * (4 * S4 + s4) + t;
-    int f;
-    const uint32_t c = scale_code(p.sf[((size_t)e * p.R + ro) * K16 + blk], f);
-    const int gs = group_slices(p.K), S = 4 * S4 + s4, grp = S / gs, s = S % gs;
-    p.out[ub * (size_t)9 * p.K + (size_t)grp * gs * 576 + (size_t)gs * 512 + (s >> 2) * 256 + lane * 8 + (s & 3) * 2 + h] =
-        (uint8_t)c;
+    const int ro0 = orig_row(rb * 16 + g, p.R, p.gate_up), ro1 = orig_row(rb * 16 + g + 8, p.R, p.gate_up);
+    const int blk = 4 * S + t;
+    const uint8_t s0 = p.sf[((size_t)e * p.R + ro0) * K16 + blk], s1 = p.sf[((size_t)e * p.R + ro1) * K16 + blk];
+    if ((s0 & 0x7Fu) == 0x7Fu || (s1 & 0x7Fu) == 0x7Fu) set_status(p.status, XCB_STATUS_NAN_SCALE);
+    uint8_t* dst = p.out + ub * (size_t)9 * p.K + (size_t)S * 576 + 512 + lane * 2;
+    dst[0] = s0;
+    dst[1] = s1;
   }
 }
 

@@ -1,38 +1,48 @@
 // Decode-path MoE kernel: one persistent launch runs (for small batches) the router, gate_up + SwiGLU (phase A),
 // down (phase B) and the weighted combine, for jobs of at most 8 tokens.  This is the HBM-bound path (T = 1
-// decode streams ~200 MB of FP4 weights for 8 experts), so the kernel is one continuous weight stream per SM:
+// decode streams ~200 MB of FP4 weights for 8 experts), so the kernel is one continuous weight stream per SM
+// whose arithmetic must keep up with HBM:
 //
-// * 19 warps per CTA, one CTA per SM, each warp one role:
-//   - warp 16 streams packed weights through a shared-memory ring (18 KB stages, one 1-D bulk copy on the TMA
-//     engine each, L2 evict-first); 18 KB copies are what a single issuing thread needs to reach HBM rate;
-//   - warp 17 stages each segment's activation rows (x for phase A, the job's SwiGLU output for phase B, after an
-//     acquire on that job's phase-A counter) into double-buffered shared memory, also with bulk copies;
-//   - warp 18 publishes finished work: one GPU-scope fence and one counter update per segment (phase A: the
-//     job's unit credits; phase B: the 16-row blocks' counts, combining a block when it completes);
-//   - warps 0..15 only compute: slice w of every 16-slice group, the GF(2) decoder (8 integer ops per 8
-//     weights), one bf16x2 multiply per register by the block-scale pair and an m16n8k16 tensor-core step fed
-//     from registers.  At T <= 8 tokens per expert the weights are used once, and staging decoded bf16 tiles
-//     through shared memory for tcgen05 would add 4 B of shared-memory traffic per weight.
-// * Units (16 output rows x full K) are reduced without a barrier: each warp drops its partial sums into a slot,
-//   the last to arrive sums the 16 partials in warp order (deterministic) and writes the epilogue.
-// * Wave schedule for few jobs: every CTA takes an equal share of every job, in the order A0 A1 B0 A2 B1 ...,
-//   so phase B of a job starts about one job after its phase A and the weight stream never waits for it.  With
-//   many jobs each CTA takes contiguous unit ranges instead.
+// * Arithmetic per 64-k slice of 16 rows (one warp): the hardware FP4 converter (cvt.rn.f16x2.e2m1x2, one
+//   instruction per two weights), one f16x2 multiply per register by the block-scale pair (itself converted from
+//   E4M3 by cvt.rn.f16x2.e4m3x2), and four m16n8k16 f16 tensor-core steps fed from registers.  Every product
+//   e2m1 * e4m3 has at most 6 significant bits and lies in [2^-10, 2688], so the f16 weight is exact.  The
+//   activations are converted to f16 once per segment in shared memory, each token scaled by a power of two
+//   2^-e chosen from its largest magnitude so that it cannot overflow f16 (e = 0 for |x| < 2^15); the epilogue
+//   multiplies the fp32 sums back by 2^e.  At T <= 8 tokens per expert the weights are used once, and a
+//   register-fed MMA reads no shared memory for them.
+// * Weight stream: warp 16 copies packed weights into a ring of 3-8 stages with 1-D bulk copies (TMA engine,
+//   L2 evict-first).  A stage holds PER consecutive slices for each of the 16 compute warps, PER chosen per
+//   phase so that a unit (16 rows x the full reduction) either spans whole stages or a stage holds whole units
+//   and no warp's slices straddle two units (DeepSeek-V3: 7 slices = 64.5 KB stages for gate_up, 4 for down).
+//   The CTA's down-projection weights are prefetched into L2 a piece per gate_up stage, so HBM sees one even
+//   stream and phase B reads L2 after the phase A -> B handoff.
+// * Partial sums leave the compute warps only at stage ends: each warp accumulates into one of two register
+//   sets, switches set at every flush point, and writes the finished set one stage later (its MMAs have long
+//   completed) or at the end of its segment, into a reduction slot.  Two epilogue warps consume the slots in order: they add the partials
+//   of each unit in warp order (deterministic), apply the epilogue (SwiGLU -> inter, or y and the post-norm
+//   sums) and hand finished units to the signalling warp.
+// * Warp 17 stages each segment's activation rows (x for phase A, the job's SwiGLU output for phase B, after an
+//   acquire on that job's phase-A counter) with bulk copies and converts them to f16 in place; warp 18 publishes
+//   finished work GPU-wide (one fence and one counter update per segment).
 // * Combine: the CTA whose phase-B units complete a 16-row block forms out = bf16(sum_s w_s * y_s) for it; with the
 //   post-norm, or for large batches, a bounded grid barrier precedes a combine spread over all CTAs.
-// * Small batches (T*k <= 256) route inside the kernel (every CTA computes the same tables), so a decode step is
-//   a single launch.  Every wait is bounded by %globaltimer; on timeout a status bit is set and the kernel drains.
+// * Small batches (T*k <= 256) route inside the kernel (every CTA computes the same tables; up to 32 routes with
+//   one warp), so a decode step is a single launch.  Every wait is bounded by %globaltimer; on timeout a status
+//   bit is set and the kernel drains.
 //
 // Reference counterpart: moe_fused's skinny path (kernels/moe_w4a16_h200/moe_w4a16.py:491-611 route,
 // :754-1133 skinny ring, :1602-1785 warp-specialised epilogues, :2617-2641 grid barrier, :2654-2796 final sum).
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "workspace.cuh"
 
 namespace xcb {
 
-// Optional timeline trace (builds with -DXCB_TRACE=1 only): %globaltimer stamps and wait counters per CTA, read back
-// with xcb_trace_read.  Off in the shipped library.
+// Optional timeline trace (builds with -DXCB_TRACE=1 only): %globaltimer stamps, clock64 spans and counters per
+// CTA, read back with xcb_trace_read.  Off in the shipped library.
 #ifndef XCB_TRACE
 #define XCB_TRACE 0
 #endif
@@ -42,109 +52,123 @@ __device__ unsigned long long g_trace[1024 * kTraceSlots];
 #define TRACE_AT(slot) (g_trace[blockIdx.x * kTraceSlots + (slot)] = gtimer())
 #define TRACE_ADD(slot, v) atomicAdd(&g_trace[blockIdx.x * kTraceSlots + (slot)], (unsigned long long)(v))
 #define TRACE_GET(slot) (*(volatile unsigned long long*)&g_trace[blockIdx.x * kTraceSlots + (slot)])
+#define TRACE_T0(name) const unsigned long long name = clock64()
+#define TRACE_SPAN(slot, name) TRACE_ADD(slot, clock64() - (name))
+#define TRACE_ONCE(slot) (TRACE_GET(slot) == 0ull ? (void)TRACE_AT(slot) : (void)0)
 #else
 #define TRACE_AT(slot) ((void)0)
 #define TRACE_ADD(slot, v) ((void)0)
+#define TRACE_T0(name) ((void)0)
+#define TRACE_SPAN(slot, name) ((void)0)
+#define TRACE_ONCE(slot) ((void)0)
 #endif
 
-#ifndef XCB_SK_NW
-#define XCB_SK_NW 16
-#endif
-constexpr int SK_NW = XCB_SK_NW;                        // compute warps (each takes slices w, w + SK_NW, ... of a group)
+constexpr int SK_NW = 16;                               // compute warps
 constexpr int SK_W_PROD = SK_NW;                        // weight producer warp
 constexpr int SK_W_ACT = SK_NW + 1;                     // activation staging warp
 constexpr int SK_W_SIG = SK_NW + 2;                     // signalling warp
 constexpr int SK_W_EPI = SK_NW + 3;                     // reduction + epilogue warps (SK_NEPI of them)
-constexpr int SK_NEPI = 2;                              // epilogue warp e takes the units with useq % SK_NEPI == e
+constexpr int SK_NEPI = 2;                              // epilogue warp e takes the flush events f with f % 2 == e
 constexpr int SK_THREADS = (SK_NW + 3 + SK_NEPI) * 32;
-constexpr int SK_SLICE_BYTES = 576;                     // 512 B of codes + 64 B of scale codes per 64-k slice
-#ifndef XCB_SK_PER
-#define XCB_SK_PER 2
-#endif
-constexpr int SK_PER = XCB_SK_PER;                      // slices per compute warp per stage
-constexpr int SK_STAGE_SLICES = SK_PER * SK_NW;         // slices per full stage (18 KB at 2 x 16)
-constexpr int SK_MAX_STAGES = 16;
-constexpr int SK_MAX_SLOTS = 4;                         // reduction slots
-constexpr int SK_SLOT_FLOATS = SK_NW * 32 * 4;
-constexpr int SK_MAX_BUFS = 2;                          // activation buffers
+constexpr int SK_SLICE = 576;                           // 512 B of codes + 64 B of scale bytes per 64-k slice
+constexpr int SK_PER_MAX = 7;                           // slices per compute warp per stage
+constexpr int SK_MAX_STAGES = 8;
+constexpr int SK_NSLOT = 2;                             // reduction slots
+constexpr int SK_NBUF_MAX = 2;                          // activation buffers
 constexpr int SK_SEG_RING = 64;                         // per-segment completion counters
-constexpr int SK_WAVE_JOBS = 0;                         // at most this many jobs: wave schedule (measured slower:
-                                                        // per-job staging and dependency stalls; kept switchable)
+constexpr int SK_WARP_ROUTES = 32;                      // up to this many routes one warp builds the tables
+constexpr int SK_COPY_SPLIT = 36864;                    // stages above this many bytes go as two bulk copies
 constexpr long long SK_L2_PREFETCH_BYTES = 96ll << 20;  // phase-B weights up to this size are prefetched into L2
 constexpr int SK_SMEM_LIMIT = 227 * 1024;
 
-// Shared-memory routing tables of the in-kernel router.
-struct SkRoute {
-  int ids[kSmallRoutes];
-  float wts[kSmallRoutes];
-  int pos[kSmallRoutes];
-  int order[kSmallRoutes];
-  int4 jobs[kSmallRoutes];
-  int counts[512];
-  int offsets[513];
-  int jcnt[512];
+// Slices per warp per stage for a unit of U slices: U % PER == 0 (a warp's slices never straddle a unit) and
+// either U % (16 PER) == 0 (a unit spans whole stages) or (16 PER) % U == 0 (a stage holds whole units).
+__host__ __device__ inline int sk_per(int U, int per_max) {
+  for (int per = per_max; per >= 1; --per)
+    if (U % per == 0 && ((16 * per) % U == 0 || U % (16 * per) == 0)) return per;
+  return 0;
+}
+
+// Control block: mbarriers and bookkeeping.
+struct SkCtl {
+  uint64_t full[SK_MAX_STAGES], empty[SK_MAX_STAGES];
+  uint64_t act_land[SK_NBUF_MAX], act_full[SK_NBUF_MAX], act_empty[SK_NBUF_MAX];
+  uint64_t slot_full[SK_NSLOT], slot_free[SK_NSLOT];
+  int seg_cnt[SK_SEG_RING];
+  int seg_gen[SK_SEG_RING];
+  int xexp[SK_NBUF_MAX][kJobTokens];  // per activation buffer and row: x was multiplied by 2^-xexp
+  int list[512];                      // 16-row blocks this CTA completed (H <= 8192)
+  int nlist;
   int njobs, nroutes;
 };
 
-// Control block: mbarriers, reduction-slot and segment bookkeeping.
-struct SkCtl {
-  uint64_t full[SK_MAX_STAGES], empty[SK_MAX_STAGES];
-  uint64_t act_full[SK_MAX_BUFS], act_empty[SK_MAX_BUFS];
-  uint64_t slot_full[SK_MAX_SLOTS];  // 16 compute warps deposited their partial sums of a unit
-  uint64_t slot_free[SK_MAX_SLOTS];  // the epilogue warp has consumed the slot
-  int seg_cnt[SK_SEG_RING];
-  int seg_gen[SK_SEG_RING];
-  float gs[2][kSmallRoutes];  // phase A / B global scale (x 2^52) of each job (jobs < kSmallRoutes; else global)
-  int list[1024];             // scratch: row blocks a segment completed
-  int nlist;
-};
-
 struct SkLayout {
-  int buf, red, route, ctl, ring, total, nstage, nbuf, nslot, rows, pitch, stage_slices;
+  int ring, buf, red, route, ctl, total;
+  int nstage, nbuf, rows, pitch, slot_bytes, perA, perB, rl, red_slot, route_cap;
 };
 
-__host__ __device__ inline SkLayout sk_layout(int H, int I, int job_tokens, int small_route) {
-  SkLayout o;
-  o.pitch = (H > I ? H : I) * 2 + 16;
-  o.rows = job_tokens < kJobTokens ? job_tokens : kJobTokens;
-  if (o.rows < 1) o.rows = 1;
-  const int route = small_route ? (int)sizeof(SkRoute) : 0;
-  o.nstage = 0;
-  // full-size stages when at least 4 fit, else half-size stages
-  for (int ss = SK_STAGE_SLICES; ss >= SK_STAGE_SLICES / 2; ss /= 2) {
-    for (int nbuf = SK_MAX_BUFS; nbuf >= 1; --nbuf) {
-      for (int nslot = SK_MAX_SLOTS; nslot >= 2; nslot /= 2) {
-        o.stage_slices = ss;
-        o.nbuf = nbuf;
-        o.nslot = nslot;
-        o.buf = 0;
-        o.red = o.buf + nbuf * o.rows * o.pitch;
-        o.route = o.red + nslot * SK_SLOT_FLOATS * 4;
+// Shared-memory plan: the weight ring (at offset 0; the many-route router's scratch aliases it before the first
+// copy), activation buffers, reduction slots, routing tables, control block.
+__host__ __device__ inline SkLayout sk_layout(int H, int I, int job_tokens, int route_R) {
+  SkLayout o{};
+  o.rows = job_tokens < 1 ? 1 : (job_tokens > kJobTokens ? kJobTokens : job_tokens);
+  o.pitch = (H > I ? H : I) * 2 + (o.rows > 1 ? 16 : 0);
+  o.rl = o.rows <= 2 ? 8 : (o.rows <= 4 ? 16 : 32);  // lanes holding useful accumulator columns (t < rl / 8)
+  o.red_slot = SK_NW * o.rl * 16;
+  o.route_cap = (route_R + 3) & ~3;
+  const int route = route_R ? o.route_cap * 32 : 0;  // ids, wts, pos, order (4 B each) + jobs (16 B)
+  for (int per_max = SK_PER_MAX; per_max >= 1; --per_max) {
+    o.perA = sk_per(H / 64, per_max);
+    o.perB = sk_per(I / 64, per_max);
+    if (!o.perA || !o.perB) break;
+    o.slot_bytes = 16 * (o.perA > o.perB ? o.perA : o.perB) * SK_SLICE;
+    for (int nbuf = SK_NBUF_MAX; nbuf >= 1; --nbuf) {
+      o.nbuf = nbuf;
+      const int rest = nbuf * o.rows * o.pitch + SK_NSLOT * o.red_slot + route + (int)sizeof(SkCtl) + 64;
+      int ns = (SK_SMEM_LIMIT - rest) / o.slot_bytes;
+      ns = ns > SK_MAX_STAGES ? SK_MAX_STAGES : ns;
+      if (ns >= 3) {
+        o.nstage = ns;
+        o.ring = 0;
+        o.buf = ns * o.slot_bytes;
+        o.red = (o.buf + nbuf * o.rows * o.pitch + 15) & ~15;
+        o.route = o.red + SK_NSLOT * o.red_slot;
         o.ctl = (o.route + route + 15) & ~15;
-        o.ring = (o.ctl + (int)sizeof(SkCtl) + 1023) & ~1023;
-        const int ns = (SK_SMEM_LIMIT - o.ring) / (ss * SK_SLICE_BYTES);
-        o.nstage = ns > SK_MAX_STAGES ? SK_MAX_STAGES : ns;
-        o.total = o.ring + o.nstage * ss * SK_SLICE_BYTES;
-        if (o.nstage >= 4) return o;
+        o.total = o.ctl + (int)sizeof(SkCtl);
+        return o;
       }
     }
   }
+  o.nstage = 0;
   return o;
 }
 
-// The units of one CTA, cut into segments of one job and one phase, in processing order.
-struct SkSegments {
-  int wave, njobs, nrbA, nrbB, G, bid;
-  long long a0, a1, b0, b1;  // contiguous mode: this CTA's unit ranges
-  int jA0, nAj, jB0, nBj;    // contiguous mode: jobs the ranges touch
+// Shared routing tables of the in-kernel router (route_cap entries each).
+struct SkTables {
+  int4* jobs;
+  int* ids;
+  float* wts;
+  int* pos;
+  int* order;
+  __device__ SkTables(uint8_t* base, int cap)
+      : jobs(reinterpret_cast<int4*>(base)),
+        ids(reinterpret_cast<int*>(base + cap * 16)),
+        wts(reinterpret_cast<float*>(base + cap * 20)),
+        pos(reinterpret_cast<int*>(base + cap * 24)),
+        order(reinterpret_cast<int*>(base + cap * 28)) {}
+};
 
-  __device__ void init(int nj, int nA_rb, int nB_rb, int grid, int b, int wave_mode) {
+// The units of one CTA, cut into segments of one job and one phase, in processing order: a contiguous share of
+// all phase-A units, then a contiguous share of all phase-B units.
+struct SkSegments {
+  int njobs, nrbA, nrbB;
+  long long a0, a1, b0, b1;  // this CTA's unit ranges
+  int jA0, nAj, jB0, nBj;    // jobs the ranges touch
+
+  __device__ void init(int nj, int nA_rb, int nB_rb, int G, int bid) {
     njobs = nj;
     nrbA = nA_rb;
     nrbB = nB_rb;
-    G = grid;
-    bid = b;
-    wave = wave_mode;
     const long long nA = (long long)njobs * nrbA, nB = (long long)njobs * nrbB;
     a0 = nA * bid / G;
     a1 = nA * (bid + 1) / G;
@@ -155,18 +179,10 @@ struct SkSegments {
     jB0 = (int)(b0 / nrbB);
     nBj = b1 > b0 ? (int)((b1 - 1) / nrbB) - jB0 + 1 : 0;
   }
-  __device__ int count() const { return wave ? 2 * njobs : nAj + nBj; }
-  // Segment i (possibly empty): phase, job, unit range [u0, u1) in the phase's unit numbering (job * nrb + rb).
+  __device__ int count() const { return nAj + nBj; }
+  // Segment i: phase, job, unit range [u0, u1) in the phase's unit numbering (job * nrb + rb).
   __device__ void at(int i, int& ph, int& job, long long& u0, long long& u1) const {
-    if (wave) {
-      if (i == 0) { ph = 0; job = 0; }
-      else if (i == 2 * njobs - 1) { ph = 1; job = njobs - 1; }
-      else if (i & 1) { ph = 0; job = (i + 1) / 2; }
-      else { ph = 1; job = (i + 1) / 2 - 1; }
-      const int nrb = ph ? nrbB : nrbA;
-      u0 = (long long)job * nrb + (long long)nrb * bid / G;
-      u1 = (long long)job * nrb + (long long)nrb * (bid + 1) / G;
-    } else if (i < nAj) {
+    if (i < nAj) {
       ph = 0;
       job = jA0 + i;
       u0 = a0 > (long long)job * nrbA ? a0 : (long long)job * nrbA;
@@ -180,30 +196,81 @@ struct SkSegments {
   }
 };
 
-// One 64-k slice for one warp: 4 packed words -> 4 tensor-core steps on two accumulator chains.  `grp` is the
-// group (ns slices: codes, then scale codes) in shared memory, s the slice within it, S its index in the unit.
-__device__ __forceinline__ void sk_slice(const uint8_t* grp, int ns, int s, const uint8_t* xrow, int S, int lane, int t,
-                                         float* acc0, float* acc1) {
-  const uint4 cw = *reinterpret_cast<const uint4*>(grp + s * 512 + lane * 16);
-  const uint32_t sc = *reinterpret_cast<const uint16_t*>(grp + ns * 512 + (s >> 2) * 256 + lane * 8 + (s & 3) * 2);
-  const uint4 xa = *reinterpret_cast<const uint4*>(xrow + S * 128 + t * 32);
-  const uint4 xb = *reinterpret_cast<const uint4*>(xrow + S * 128 + t * 32 + 16);
-  const uint32_t s2 = scale_pair(sc);
-  uint32_t r0, r1, r2, r3;
-  decode_fp4x8(cw.x, r0, r1, r2, r3);
-  mma_16816(acc0, bf16x2_mul_lo(r0, s2), bf16x2_mul_hi(r1, s2), bf16x2_mul_lo(r2, s2), bf16x2_mul_hi(r3, s2), xa.x, xa.y);
-  decode_fp4x8(cw.y, r0, r1, r2, r3);
-  mma_16816(acc1, bf16x2_mul_lo(r0, s2), bf16x2_mul_hi(r1, s2), bf16x2_mul_lo(r2, s2), bf16x2_mul_hi(r3, s2), xa.z, xa.w);
-  decode_fp4x8(cw.z, r0, r1, r2, r3);
-  mma_16816(acc0, bf16x2_mul_lo(r0, s2), bf16x2_mul_hi(r1, s2), bf16x2_mul_lo(r2, s2), bf16x2_mul_hi(r3, s2), xb.x, xb.y);
-  decode_fp4x8(cw.w, r0, r1, r2, r3);
-  mma_16816(acc1, bf16x2_mul_lo(r0, s2), bf16x2_mul_hi(r1, s2), bf16x2_mul_lo(r2, s2), bf16x2_mul_hi(r3, s2), xb.z, xb.w);
+// ------------------------------------------------------------------------------------------------ arithmetic
+__device__ __forceinline__ void cvt_e2m1x8(uint32_t q, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n cvt.rn.f16x2.e2m1x2 %2, b2;\n"
+      " cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+      : "r"(q));
+}
+// Two E4M3 scale bytes (row g in the low byte, row g + 8 in the high byte) -> f16x2.
+__device__ __forceinline__ uint32_t cvt_e4m3x2(uint32_t two) {
+  uint32_t s;
+  asm("{\n .reg .b16 h;\n cvt.u16.u32 h, %1;\n cvt.rn.f16x2.e4m3x2 %0, h;\n}" : "=r"(s) : "r"(two));
+  return s;
+}
+__device__ __forceinline__ void mma_16816_f16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                              uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t h2mul_lo(uint32_t a, uint32_t s) {  // a * (s.lo, s.lo)
+  __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), __low2half2(*reinterpret_cast<__half2*>(&s)));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t h2mul_hi(uint32_t a, uint32_t s) {  // a * (s.hi, s.hi)
+  __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), __high2half2(*reinterpret_cast<__half2*>(&s)));
+  return *reinterpret_cast<uint32_t*>(&r);
 }
 
-// In-kernel router for T*k <= kSmallRoutes (all warps; every CTA computes the same tables).
-__device__ void sk_route_small(const SkinnyParams& p, SkRoute& r) {
+// One 64-k slice of one unit for one warp: lane (g, t) holds the codes of rows g and g + 8 at k = 16t + 4i + 0..3
+// of the slice for step i, and the scale pair of block t; xs = the f16 activation row at the slice's first k.
+__device__ __forceinline__ void sk_slice(const uint8_t* sl, const uint8_t* xs, int lane, int t, float* acc0,
+                                         float* acc1) {
+  const uint4 cw = *reinterpret_cast<const uint4*>(sl + lane * 16);
+  const uint32_t sc = *reinterpret_cast<const uint16_t*>(sl + 512 + lane * 2);
+  const uint4 xa = *reinterpret_cast<const uint4*>(xs + t * 32);
+  const uint4 xb = *reinterpret_cast<const uint4*>(xs + t * 32 + 16);
+  const uint32_t s2 = cvt_e4m3x2(sc);
+  uint32_t r0, r1, r2, r3;
+  cvt_e2m1x8(cw.x, r0, r1, r2, r3);
+  mma_16816_f16(acc0, h2mul_lo(r0, s2), h2mul_hi(r1, s2), h2mul_lo(r2, s2), h2mul_hi(r3, s2), xa.x, xa.y);
+  cvt_e2m1x8(cw.y, r0, r1, r2, r3);
+  mma_16816_f16(acc1, h2mul_lo(r0, s2), h2mul_hi(r1, s2), h2mul_lo(r2, s2), h2mul_hi(r3, s2), xa.z, xa.w);
+  cvt_e2m1x8(cw.z, r0, r1, r2, r3);
+  mma_16816_f16(acc0, h2mul_lo(r0, s2), h2mul_hi(r1, s2), h2mul_lo(r2, s2), h2mul_hi(r3, s2), xb.x, xb.y);
+  cvt_e2m1x8(cw.w, r0, r1, r2, r3);
+  mma_16816_f16(acc1, h2mul_lo(r0, s2), h2mul_hi(r1, s2), h2mul_lo(r2, s2), h2mul_hi(r3, s2), xb.z, xb.w);
+}
+
+// PER consecutive slices of one warp into one accumulator pair (compile-time PER so the slices interleave).
+template <int PER>
+__device__ __forceinline__ void sk_run(const uint8_t* sl, const uint8_t* xs, int lane, int t, float* acc0, float* acc1) {
+#pragma unroll
+  for (int j = 0; j < PER; ++j) sk_slice(sl + j * SK_SLICE, xs + j * 128, lane, t, acc0, acc1);
+}
+__device__ __forceinline__ void sk_run_per(int per, const uint8_t* sl, const uint8_t* xs, int lane, int t, float* a0,
+                                           float* a1) {
+  switch (per) {
+    case 7: sk_run<7>(sl, xs, lane, t, a0, a1); break;
+    case 6: sk_run<6>(sl, xs, lane, t, a0, a1); break;
+    case 5: sk_run<5>(sl, xs, lane, t, a0, a1); break;
+    case 4: sk_run<4>(sl, xs, lane, t, a0, a1); break;
+    case 3: sk_run<3>(sl, xs, lane, t, a0, a1); break;
+    case 2: sk_run<2>(sl, xs, lane, t, a0, a1); break;
+    default: sk_run<1>(sl, xs, lane, t, a0, a1); break;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ router
+// In-kernel router for T*k <= kSmallRoutes (every CTA computes the same tables).  `scratch` (the ring, unused
+// yet) holds the per-expert counts of the many-route variant.
+__device__ void sk_route_small(const SkinnyParams& p, SkTables& rt, SkCtl& cb, int* scratch) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
   const int R = p.T * p.k;
+  const int JC = p.job_tokens;  // tokens per job
   for (int t = warp; t < p.T; t += nthr / 32) {
     int id = -1;
     float w = 0.f;
@@ -218,85 +285,162 @@ __device__ void sk_route_small(const SkinnyParams& p, SkRoute& r) {
       }
     }
     if (lane < p.k) {
-      r.ids[t * p.k + lane] = id;
-      r.wts[t * p.k + lane] = w;
+      rt.ids[t * p.k + lane] = id;
+      rt.wts[t * p.k + lane] = w;
     }
   }
   __syncthreads();
   if (tid == 0) TRACE_AT(15);
-  // per-expert counts and each route's rank among the earlier routes of its expert (stable order)
-  for (int e = tid; e < p.E_loc; e += nthr) {
-    int c = 0;
-    for (int f = 0; f < R; ++f) c += (r.ids[f] == p.lo + e);
-    r.counts[e] = c;
-    r.offsets[e] = c;
-    r.jcnt[e] = (c + kJobTokens - 1) / kJobTokens;
-  }
-  for (int f = tid; f < R; f += nthr) {
-    const int id = r.ids[f];
-    int rank = 0;
-    for (int g = 0; g < f; ++g) rank += (r.ids[g] == id);
-    r.pos[f] = rank;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    const int tot = warp_exclusive_scan(r.offsets, p.E_loc);
-    if (lane == 0) {
-      r.nroutes = tot;
-      r.offsets[p.E_loc] = tot;
+  if (R <= SK_WARP_ROUTES) {
+    // one warp: lane f owns route f; ranks by __match_any_sync, offsets and job bases by a 32-step scan
+    if (warp == 0) {
+      int el = -1;
+      if (lane < R) {
+        const int id = rt.ids[lane];
+        el = id - p.lo;
+        if (id < 0 || el < 0 || el >= p.E_loc) el = -1;
+      }
+      const uint32_t peers = __match_any_sync(0xffffffffu, el);
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      const int cnt = __popc(peers);
+      int less = 0, jbase = 0;
+      for (int g2 = 0; g2 < 32; ++g2) {
+        const int eg = __shfl_sync(0xffffffffu, el, g2);
+        const int cg = __shfl_sync(0xffffffffu, cnt, g2);
+        const int rg = __shfl_sync(0xffffffffu, rank, g2);
+        if (eg >= 0 && el >= 0 && eg < el) {
+          ++less;
+          if (rg == 0) jbase += (cg + JC - 1) / JC;
+        }
+      }
+      const bool lead = el >= 0 && rank == 0;
+      const int nj = lead ? (cnt + JC - 1) / JC : 0;
+      if (lane < R) {
+        rt.pos[lane] = el >= 0 ? less + rank : -1;
+        if (el >= 0) rt.order[less + rank] = lane;
+      }
+      for (int i = 0; i < nj; ++i) rt.jobs[jbase + i] = make_int4(el, less + JC * i, min(JC, cnt - JC * i), 0);
+      const int njobs = __reduce_add_sync(0xffffffffu, nj);
+      const int nroutes = __popc(__ballot_sync(0xffffffffu, el >= 0));
+      if (lane == 0) {
+        cb.njobs = njobs;
+        cb.nroutes = nroutes;
+      }
     }
-  } else if (warp == 1) {
-    const int tot = warp_exclusive_scan(r.jcnt, p.E_loc);
-    if (lane == 0) r.njobs = tot;
-  }
-  __syncthreads();
-  if (tid == 0) TRACE_AT(16);
-  for (int f = tid; f < R; f += nthr) {
-    const int el = r.ids[f] - p.lo;
-    if (r.ids[f] >= 0 && el >= 0 && el < p.E_loc) {
-      const int q = r.offsets[el] + r.pos[f];
-      r.pos[f] = q;
-      r.order[q] = f;
-    } else {
-      r.pos[f] = -1;
+  } else {
+    int* counts = scratch;              // [E_loc]
+    int* offs = counts + p.E_loc;       // [E_loc + 1]
+    int* jcnt = offs + p.E_loc + 1;     // [E_loc]
+    for (int e = tid; e < p.E_loc; e += nthr) {
+      int c = 0;
+      for (int f = 0; f < R; ++f) c += (rt.ids[f] == p.lo + e);
+      counts[e] = c;
+      offs[e] = c;
+      jcnt[e] = (c + JC - 1) / JC;
     }
-  }
-  for (int e = tid; e < p.E_loc; e += nthr) {
-    const int c = r.counts[e];
-    int j = r.jcnt[e];
-    for (int s0 = 0; s0 < c; s0 += kJobTokens, ++j) r.jobs[j] = make_int4(e, r.offsets[e] + s0, min(kJobTokens, c - s0), 0);
+    for (int f = tid; f < R; f += nthr) {
+      const int id = rt.ids[f];
+      int rank = 0;
+      for (int g2 = 0; g2 < f; ++g2) rank += (rt.ids[g2] == id);
+      rt.pos[f] = rank;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const int tot = warp_exclusive_scan(offs, p.E_loc);
+      if (lane == 0) {
+        cb.nroutes = tot;
+        offs[p.E_loc] = tot;
+      }
+    } else if (warp == 1) {
+      const int tot = warp_exclusive_scan(jcnt, p.E_loc);
+      if (lane == 0) cb.njobs = tot;
+    }
+    __syncthreads();
+    for (int f = tid; f < R; f += nthr) {
+      const int el = rt.ids[f] - p.lo;
+      if (rt.ids[f] >= 0 && el >= 0 && el < p.E_loc) {
+        const int q = offs[el] + rt.pos[f];
+        rt.pos[f] = q;
+        rt.order[q] = f;
+      } else {
+        rt.pos[f] = -1;
+      }
+    }
+    for (int e = tid; e < p.E_loc; e += nthr) {
+      const int c = counts[e];
+      int j = jcnt[e];
+      for (int s0 = 0; s0 < c; s0 += JC, ++j) rt.jobs[j] = make_int4(e, offs[e] + s0, min(JC, c - s0), 0);
+    }
   }
   __syncthreads();
   if (blockIdx.x == 0) {  // publish the routing (tests and callers read it from the workspace)
     for (int f = tid; f < R; f += nthr) {
-      p.g_ids[f] = r.ids[f];
-      p.g_wts[f] = r.wts[f];
-      p.g_pos[f] = r.pos[f];
-      if (p.ids_out) p.ids_out[f] = r.ids[f];
-      if (p.wts_out) p.wts_out[f] = r.wts[f];
+      p.g_ids[f] = rt.ids[f];
+      p.g_wts[f] = rt.wts[f];
+      p.g_pos[f] = rt.pos[f];
+      if (p.ids_out) p.ids_out[f] = rt.ids[f];
+      if (p.wts_out) p.wts_out[f] = rt.wts[f];
     }
-    for (int q = tid; q < r.nroutes; q += nthr) p.g_order[q] = r.order[q];
+    for (int q = tid; q < cb.nroutes; q += nthr) p.g_order[q] = rt.order[q];
     for (int e = tid; e <= p.E_loc; e += nthr) {
-      if (e < p.E_loc) p.g_counts[e] = r.counts[e];
-      p.g_offsets[e] = r.offsets[e];
+      int c = 0, below = 0;
+      for (int f = 0; f < R; ++f) {
+        const int id = rt.ids[f], el = id - p.lo;
+        if (id >= 0 && el >= 0 && el < p.E_loc) {
+          c += (el == e);
+          below += (el < e);
+        }
+      }
+      if (e < p.E_loc) p.g_counts[e] = c;
+      p.g_offsets[e] = below;
     }
   }
 }
 
-
-
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Convert `ntok` staged bf16 rows of K values to f16 in place (one warp), each row scaled by 2^-e with e chosen
+// from its largest magnitude so that the result cannot overflow f16; e is returned per row in xexp.
+__device__ void sk_rows_to_f16(uint8_t* buf, int pitch, int ntok, int K, int* xexp) {
+  const int lane = threadIdx.x & 31, nv = K / 8;
+  for (int n = 0; n < ntok; ++n) {
+    uint4* row = reinterpret_cast<uint4*>(buf + (size_t)n * pitch);
+    uint32_t m = 0;
+    for (int v = lane; v < nv; v += 32) {
+      const uint4 q = row[v];
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) m = max(m, max(w[i] & 0x7FFFu, (w[i] >> 16) & 0x7FFFu));
+    }
+    m = __reduce_max_sync(0xffffffffu, m);
+    const int E = (int)(m >> 7);           // bf16 exponent field of the largest magnitude: |x| < 2^(E - 126)
+    const int e = E > 141 ? E - 141 : 0;   // scaled magnitudes stay below 2^15
+    const float sc = __uint_as_float((uint32_t)(127 - e) << 23);
+    for (int v = lane; v < nv; v += 32) {
+      const uint4 q = row[v];
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __half2 h = __floats2half2_rn(__uint_as_float(w[i] << 16) * sc, __uint_as_float(w[i] & 0xFFFF0000u) * sc);
+        o[i] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      row[v] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    if (lane == 0) xexp[n] = e;
+  }
+}
 
 __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  const SkLayout L = sk_layout(p.H, p.I, p.job_tokens, p.small_route);
+  const SkLayout L = sk_layout(p.H, p.I, p.job_tokens, p.small_route ? p.T * p.k : 0);
+  uint8_t* ring = smem + L.ring;
   uint8_t* bufs = smem + L.buf;
   float* red = reinterpret_cast<float*>(smem + L.red);
-  SkRoute& rt = *reinterpret_cast<SkRoute*>(smem + L.route);
   SkCtl& cb = *reinterpret_cast<SkCtl*>(smem + L.ctl);
-  uint8_t* ring = smem + L.ring;
+  SkTables rt(smem + L.route, L.route_cap);
   int* status = p.ctl + kCtlStatus;
-  const int NST = L.nstage, NBUF = L.nbuf, NSLOT = L.nslot;
+  const int NST = L.nstage, NBUF = L.nbuf;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, bid = blockIdx.x;
 
@@ -307,49 +451,38 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
       mbar_init(cb.empty + i, SK_NW);
     }
     for (int i = 0; i < NBUF; ++i) {
+      mbar_init(cb.act_land + i, 1);
       mbar_init(cb.act_full + i, 1);
       mbar_init(cb.act_empty + i, SK_NW);
     }
-    fence_mbar_init();
-  }
-  if (tid == 0) {
-    for (int i = 0; i < NSLOT; ++i) {
+    for (int i = 0; i < SK_NSLOT; ++i) {
       mbar_init(cb.slot_full + i, SK_NW);
       mbar_init(cb.slot_free + i, 1);
     }
     fence_mbar_init();
+    cb.nlist = 0;
   }
   for (int i = tid; i < SK_SEG_RING; i += SK_THREADS) {
     cb.seg_cnt[i] = 0;
     cb.seg_gen[i] = 0;
   }
-  if (tid == 0) cb.nlist = 0;
-  if (p.small_route) sk_route_small(p, rt);
+  if (p.small_route) {
+    sk_route_small(p, rt, cb, reinterpret_cast<int*>(ring));
+  }
   __syncthreads();
   if (tid == 0) TRACE_AT(1);
 
-  const int njobs = p.small_route ? rt.njobs : p.ctl[kCtlJobs];
+  const int njobs = p.small_route ? cb.njobs : p.ctl[kCtlJobs];
   const int4* jobs = p.small_route ? rt.jobs : p.jobs;
   const int* order = p.small_route ? rt.order : p.order;
   const int* pos = p.small_route ? rt.pos : p.pos;
   const float* wts = p.small_route ? rt.wts : p.wts;
   const int nrbA = (2 * p.I) / 16, nrbB = p.H / 16;
-  const int nSA = p.H / 64, nSB = p.I / 64;  // slices per unit
-  const int gsA = group_slices(p.H), gsB = group_slices(p.I);
-  const int ssA = L.stage_slices / gsA * gsA, ssB = L.stage_slices / gsB * gsB;  // slices per full stage (whole groups)
+  const int UA = p.H / 64, UB = p.I / 64;  // slices per unit
   const size_t unitA = (size_t)9 * p.H, unitB = (size_t)9 * p.I;
   SkSegments segs;
-  segs.init(njobs, nrbA, nrbB, G, bid, njobs <= SK_WAVE_JOBS);
+  segs.init(njobs, nrbA, nrbB, G, bid);
   const int nseg = segs.count();
-  const bool gs_cached = njobs <= kSmallRoutes;
-  if (gs_cached) {
-    for (int j = tid; j < njobs; j += SK_THREADS) {
-      const int e = jobs[j].x;
-      cb.gs[0][j] = p.gsA[e] * kTwo52;
-      cb.gs[1][j] = p.gsB[e] * kTwo52;
-    }
-  }
-  __syncthreads();
 
   if (warp == SK_W_PROD) {
     // ------------------------------------------------------------------ weight producer
@@ -357,76 +490,109 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
       const uint64_t pol = policy_evict_first();
       int it = 0;
       bool ok = true;
-      // phase-B weights do not depend on phase A: when they fit in L2, stream them into L2 right behind this CTA's
-      // phase-A weights, so HBM sees one continuous stream and phase B reads L2 after the A -> B handoff
+      // phase-B weights do not depend on phase A: when they fit in L2, this CTA's share is prefetched into L2 a
+      // piece per phase-A stage (so HBM sees one even stream) and phase B reads L2 after the A -> B handoff
       const bool prefetch_b = (long long)njobs * nrbB * (long long)unitB <= SK_L2_PREFETCH_BYTES;
-      bool prefetched = false;
+      int pf_seg = segs.nAj;           // next phase-B segment to prefetch
+      size_t pf_off = 0;               // bytes of it already prefetched
+      size_t pf_step = 0;              // bytes per phase-A stage
+      if (prefetch_b && segs.nAj > 0) {
+        const long long nA = segs.a1 - segs.a0, nB = segs.b1 - segs.b0;
+        const long long stagesA = (nA * UA + 16 * L.perA - 1) / (16 * L.perA) + segs.nAj;
+        pf_step = (size_t)((nB * (long long)unitB + stagesA - 1) / stagesA + 4095) & ~(size_t)4095;
+      }
+      auto prefetch_b_bytes = [&](size_t budget) {  // issue up to `budget` bytes of the remaining phase-B share
+        while (budget > 0 && pf_seg < nseg) {
+          int ph2, job2;
+          long long v0, v1;
+          segs.at(pf_seg, ph2, job2, v0, v1);
+          const size_t total = v1 > v0 ? (size_t)(v1 - v0) * unitB : 0;  // consecutive units are contiguous
+          if (pf_off >= total) {
+            ++pf_seg;
+            pf_off = 0;
+            continue;
+          }
+          const uint8_t* first = p.wB + ((size_t)jobs[job2].x * nrbB + (size_t)(v0 - (long long)job2 * nrbB)) * unitB;
+          const size_t n = min(min(total - pf_off, budget), (size_t)1 << 20);
+          bulk_prefetch_l2(first + pf_off, (uint32_t)n);
+          pf_off += n;
+          budget -= n;
+        }
+      };
       for (int s = 0; s < nseg && ok; ++s) {
         int ph, job;
         long long u0, u1;
         segs.at(s, ph, job, u0, u1);
-        if (ph == 1 && prefetch_b && !prefetched) {
-          prefetched = true;
-          for (int s2 = s; s2 < nseg; ++s2) {
-            int ph2, job2;
-            long long v0, v1;
-            segs.at(s2, ph2, job2, v0, v1);
-            if (ph2 != 1 || v1 <= v0) continue;
-            const uint8_t* first = p.wB + ((size_t)jobs[job2].x * nrbB + (size_t)(v0 - (long long)job2 * nrbB)) * unitB;
-            const size_t total = (size_t)(v1 - v0) * unitB;  // consecutive units of one job are contiguous
-            for (size_t off = 0; off < total; off += (size_t)1 << 20)
-              bulk_prefetch_l2(first + off, (uint32_t)min(total - off, (size_t)1 << 20));
-          }
-        }
-        // the segment's units are one contiguous byte range; stream it in stages of whole groups
-        const int nrb = ph ? nrbB : nrbA, ss = ph ? ssB : ssA;
-        const long long nsl = (u1 - u0) * (ph ? nSB : nSA);
+        if (u1 <= u0) continue;
+        if (ph == 1 && prefetch_b) prefetch_b_bytes((size_t)-1);  // whatever phase A did not cover
+        const int nrb = ph ? nrbB : nrbA, U = ph ? UB : UA, SS = 16 * (ph ? L.perB : L.perA);
+        const int nsl = (int)(u1 - u0) * U;
         const uint8_t* seg = (ph ? p.wB : p.wA) +
                              ((size_t)jobs[job].x * nrb + (size_t)(u0 - (long long)job * nrb)) * (ph ? unitB : unitA);
-        for (long long base = 0; base < nsl && ok; base += ss, ++it) {
-          const int ns = (int)min((long long)ss, nsl - base);
+        for (int base = 0; base < nsl; base += SS, ++it) {
+          const uint32_t bytes = (uint32_t)min(SS, nsl - base) * SK_SLICE;
           const int st = it % NST;
+          TRACE_T0(t_e);
           if (it >= NST && !mbar_wait(cb.empty + st, ((it / NST) + 1) & 1, p.timeout_ns, status)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(cb.full + st, ns * SK_SLICE_BYTES);
-          bulk_g2s_stream(ring + (size_t)st * L.stage_slices * SK_SLICE_BYTES, seg + (size_t)base * SK_SLICE_BYTES,
-                          ns * SK_SLICE_BYTES, cb.full + st, pol);
+          TRACE_SPAN(13, t_e);
+          uint8_t* dst = ring + (size_t)st * L.slot_bytes;
+          const uint8_t* src = seg + (size_t)base * SK_SLICE;
+          mbar_arrive_expect_tx(cb.full + st, bytes);
+          if (bytes > (uint32_t)SK_COPY_SPLIT) {
+            const uint32_t h = (bytes / 2 + 15u) & ~15u;
+            bulk_g2s_stream(dst, src, h, cb.full + st, pol);
+            bulk_g2s_stream(dst + h, src + h, bytes - h, cb.full + st, pol);
+          } else {
+            bulk_g2s_stream(dst, src, bytes, cb.full + st, pol);
+          }
+          if (ph == 0 && prefetch_b) prefetch_b_bytes(pf_step);
         }
       }
       TRACE_AT(3);
       for (int i = max(0, it - NST); i < it; ++i) mbar_wait(cb.full + (i % NST), (i / NST) & 1, p.timeout_ns, status);
     }
   } else if (warp == SK_W_ACT) {
-    // ------------------------------------------------------------------ activation staging
-    if (lane == 0) {
-      int k = 0;  // non-empty segments so far
-      for (int s = 0; s < nseg; ++s) {
-        int ph, job;
-        long long u0, u1;
-        segs.at(s, ph, job, u0, u1);
-        if (u1 <= u0) continue;
-        const int b = k % NBUF;
+    // ------------------------------------------------------------------ activation staging + f16 conversion
+    int k = 0;  // non-empty segments so far
+    for (int s = 0; s < nseg; ++s) {
+      int ph, job;
+      long long u0, u1;
+      segs.at(s, ph, job, u0, u1);
+      if (u1 <= u0) continue;
+      const int b = k % NBUF;
+      const int4 jb = jobs[job];
+      const int K = ph ? p.I : p.H;
+      const int ntok = min(jb.z, L.rows);
+      uint8_t* dst = bufs + (size_t)b * L.rows * L.pitch;
+      if (lane == 0) {
         if (k >= NBUF) mbar_wait(cb.act_empty + b, ((k / NBUF) + 1) & 1, p.timeout_ns, status);
-        const int4 jb = jobs[job];
-        const int K = ph ? p.I : p.H;
         if (ph == 1) {
+          TRACE_ONCE(5);
           wait_geq(p.doneA + job, nrbA, p.timeout_ns, status);  // every phase-A unit of this job is published
+          TRACE_ONCE(6);
           fence_proxy_async_global();
         }
-        uint8_t* dst = bufs + (size_t)b * L.rows * L.pitch;
-        const int ntok = min(jb.z, L.rows);
-        mbar_arrive_expect_tx(cb.act_full + b, ntok * K * 2);
+        mbar_arrive_expect_tx(cb.act_land + b, ntok * K * 2);
         for (int n = 0; n < ntok; ++n) {
           const uint16_t* src = ph ? p.inter + (size_t)(jb.y + n) * p.I : p.x + (size_t)(order[jb.y + n] / p.k) * p.H;
-          bulk_g2s(dst + n * (size_t)(K * 2 + 16), src, K * 2, cb.act_full + b);
+          bulk_g2s(dst + (size_t)n * L.pitch, src, K * 2, cb.act_land + b);
         }
-        ++k;
       }
-      for (int i = max(0, k - NBUF); i < k; ++i) mbar_wait(cb.act_full + (i % NBUF), (i / NBUF) & 1, p.timeout_ns, status);
-      TRACE_AT(20);
+      __syncwarp();
+      mbar_wait(cb.act_land + b, (k / NBUF) & 1, p.timeout_ns, status);
+      if (lane == 0) TRACE_ONCE(17);
+      sk_rows_to_f16(dst, L.pitch, ntok, K, cb.xexp[b]);
+      __syncwarp();
+      if (lane == 0) {
+        TRACE_ONCE(16);
+        mbar_arrive(cb.act_full + b);
+      }
+      ++k;
     }
+    if (lane == 0) TRACE_AT(20);
   } else if (warp == SK_W_SIG) {
     // ------------------------------------------------------------------ signalling
     int k = 0;
@@ -437,7 +603,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
       if (u1 <= u0) continue;
       const int slot = k % SK_SEG_RING;
       const int want = (int)(u1 - u0);
-      // all units of the segment reduced and written by the compute warps (CTA-scope release, acquire here)
+      // all units of the segment reduced and written by the epilogue warps (CTA-scope release, acquire here)
       if (lane == 0) {
         const uint64_t t0 = gtimer();
         while (*reinterpret_cast<volatile int*>(&cb.seg_cnt[slot]) < want) {
@@ -449,7 +615,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
         }
       }
       __syncwarp();
-      __threadfence();  // cumulative: publishes the compute warps' epilogue writes GPU-wide before the counters move
+      __threadfence();  // cumulative: publishes the epilogue writes GPU-wide before the counters move
       if (lane == 0) {
         cb.seg_cnt[slot] = 0;
         *reinterpret_cast<volatile int*>(&cb.seg_gen[slot]) = k / SK_SEG_RING + 1;
@@ -469,82 +635,101 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
     if (lane == 0) TRACE_AT(21);
   } else if (warp >= SK_W_EPI) {
     // ------------------------------------------------------------------ reduction + epilogue
-    const int g = lane >> 2, t = lane & 3;
+    // slot lane l holds the partial of accumulator lane (g, t) = (l % 8, l / 8): rows g, g + 8; tokens 2t, 2t + 1
     const int epi = warp - SK_W_EPI;
-    int useq = 0, k = 0;
+    const int g = lane & 7, t = lane >> 3;
+    const bool act = lane < L.rl;
+    int f = 0, k = 0;
     for (int s = 0; s < nseg; ++s) {
       int ph, job;
       long long u0, u1;
       segs.at(s, ph, job, u0, u1);
       if (u1 <= u0) continue;
-      const int nrb = ph ? nrbB : nrbA;
+      const int nrb = ph ? nrbB : nrbA, U = ph ? UB : UA, PER = ph ? L.perB : L.perA, SS = 16 * PER;
+      const int nunits = (int)(u1 - u0);
       const int4 jb = jobs[job];
-      const float gsc = gs_cached ? cb.gs[ph][job] : (ph ? p.gsB : p.gsA)[jb.x] * kTwo52;
-      for (long long u = u0; u < u1; ++u, ++useq) {
-        if (useq % SK_NEPI != epi) continue;
-        const int rb = (int)(u - (long long)job * nrb);
-        const int slot = useq % NSLOT;
-        mbar_wait(cb.slot_full + slot, (useq / NSLOT) & 1, p.timeout_ns, status);
-        const float* sb = red + slot * SK_SLOT_FLOATS;
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-        for (int w = 0; w < SK_NW; ++w) {  // fixed warp order: deterministic sums
-          const float4 r = *reinterpret_cast<const float4*>(sb + (w * 32 + lane) * 4);
-          v[0] += r.x; v[1] += r.y; v[2] += r.z; v[3] += r.w;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(cb.slot_free + slot);
-        if (ph == 0) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int n = 2 * t + h;
-            if (n < jb.z) {
-              const float gt = v[h] * gsc, up = v[2 + h] * gsc;
-              const float hv = __fdividef(gt, 1.f + __expf(-gt)) * up;  // SiLU(g) * u (fast exp / divide)
-              p.inter[(size_t)(jb.y + n) * p.I + rb * 8 + g] = f2bf(hv);
-            }
-          }
-        } else {
-          const int r0 = rb * 16 + g, r1 = r0 + 8;
-          float n0 = 1.f, n1 = 1.f;
-          if (p.post_norm) {
-            n0 += bf2f(p.normw[r0]);
-            n1 += bf2f(p.normw[r1]);
-          }
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int n = 2 * t + h;
-            const float y0 = v[h] * gsc * n0, y1 = v[2 + h] * gsc * n1;
-            float sq = y0 * y0 + y1 * y1;
-            if (n < jb.z) {
-              p.y[(size_t)(jb.y + n) * p.H + r0] = y0;
-              p.y[(size_t)(jb.y + n) * p.H + r1] = y1;
-            }
-            if (p.post_norm) {
-              sq += __shfl_xor_sync(0xffffffffu, sq, 4);
-              sq += __shfl_xor_sync(0xffffffffu, sq, 8);
-              sq += __shfl_xor_sync(0xffffffffu, sq, 16);
-              if (g == 0 && n < jb.z) atomicAdd(p.ss + jb.y + n, sq);
-            }
-          }
-        }
-        // hand the finished unit to the signalling warp (CTA-scope release of the epilogue writes)
-        __syncwarp();
+      const float gsc = (ph ? p.gsB : p.gsA)[jb.x];
+      const int upe = U >= SS ? 1 : SS / U;            // units per flush event
+      const int wpu = U >= SS ? SK_NW : U / PER;       // contributing warps per unit
+      const int nev = (nunits + upe - 1) / upe;
+      for (int ev = 0; ev < nev; ++ev, ++f) {
+        if (f % SK_NEPI != epi) continue;
+        const int slot = f % SK_NSLOT;
+        TRACE_T0(t_sl);
+        mbar_wait(cb.slot_full + slot, (f / SK_NSLOT) & 1, p.timeout_ns, status);
         if (lane == 0) {
-          const int sl = k % SK_SEG_RING;
-          const int want = k / SK_SEG_RING;
-          if (*reinterpret_cast<volatile int*>(&cb.seg_gen[sl]) < want) {
-            const uint64_t t0 = gtimer();
-            while (*reinterpret_cast<volatile int*>(&cb.seg_gen[sl]) < want) {
-              __nanosleep(100);
-              if (gtimer() - t0 > p.timeout_ns) {
-                set_status(status, XCB_STATUS_DEVICE_TIMEOUT);
-                break;
+          TRACE_SPAN(24, t_sl);
+          TRACE_ADD(26, 1);
+        }
+        const float* sb = red + slot * (L.red_slot / 4);
+        const int i0 = ev * upe, i1 = min(nunits, i0 + upe);
+        for (int i = i0; i < i1; ++i) {
+          const int w0 = (i - i0) * wpu;
+          float v[4] = {0.f, 0.f, 0.f, 0.f};
+          if (act) {
+            for (int w = w0; w < w0 + wpu; ++w) {  // fixed warp order: deterministic sums
+              const float4 r = *reinterpret_cast<const float4*>(sb + (w * L.rl + lane) * 4);
+              v[0] += r.x; v[1] += r.y; v[2] += r.z; v[3] += r.w;
+            }
+          }
+          if (i + 1 == i1) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(cb.slot_free + slot);
+          }
+          const int rb = (int)(u0 + i - (long long)job * nrb);
+          if (ph == 0) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int n = 2 * t + h;
+              if (act && n < jb.z) {
+                const float gt = v[h] * gsc, up = v[2 + h] * gsc;
+                const float hv = __fdividef(gt, 1.f + __expf(-gt)) * up;  // SiLU(g) * u (fast exp / divide)
+                p.inter[(size_t)(jb.y + n) * p.I + rb * 8 + g] = f2bf(hv);
+              }
+            }
+          } else {
+            const int r0 = rb * 16 + g, r1 = r0 + 8;
+            float n0 = 1.f, n1 = 1.f;
+            if (p.post_norm) {
+              n0 += bf2f(p.normw[r0]);
+              n1 += bf2f(p.normw[r1]);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int n = 2 * t + h;
+              const bool ok = act && n < jb.z;
+              const float y0 = v[h] * gsc * n0, y1 = v[2 + h] * gsc * n1;
+              if (ok) {
+                p.y[(size_t)(jb.y + n) * p.H + r0] = y0;
+                p.y[(size_t)(jb.y + n) * p.H + r1] = y1;
+              }
+              if (p.post_norm) {
+                float sq = ok ? y0 * y0 + y1 * y1 : 0.f;
+                sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+                sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+                sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+                if (g == 0 && ok) atomicAdd(p.ss + jb.y + n, sq);
               }
             }
           }
-          __threadfence_block();
-          atomicAdd(&cb.seg_cnt[sl], 1);
+          // hand the finished unit to the signalling warp (CTA-scope release of the epilogue writes)
+          __syncwarp();
+          if (lane == 0) {
+            const int sl = k % SK_SEG_RING;
+            const int want = k / SK_SEG_RING;
+            if (*reinterpret_cast<volatile int*>(&cb.seg_gen[sl]) < want) {
+              const uint64_t t0 = gtimer();
+              while (*reinterpret_cast<volatile int*>(&cb.seg_gen[sl]) < want) {
+                __nanosleep(100);
+                if (gtimer() - t0 > p.timeout_ns) {
+                  set_status(status, XCB_STATUS_DEVICE_TIMEOUT);
+                  break;
+                }
+              }
+            }
+            __threadfence_block();
+            atomicAdd(&cb.seg_cnt[sl], 1);
+          }
         }
       }
       ++k;
@@ -552,26 +737,33 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
     if (lane == 0) TRACE_AT(22);
   } else {
     // ------------------------------------------------------------------ compute warps
-    // A segment's slices are streamed in stages of whole groups; warp w takes stage slices w, w + SK_NW, ...
-    // Each slice belongs to one unit (its 16 rows); a warp hands its partial sums of a unit to the epilogue warps
-    // when its slices move past the unit (a unit none of whose slices this warp saw gets a zero partial).
+    // Stage i of a segment holds slices [i SS, i SS + ns); warp w takes [i SS + w PER, + PER), all in one unit.
+    // Two accumulator sets alternate at every flush point; the finished set is written one stage later.
     const int g = lane >> 2, t = lane & 3;
-    const int grow = g < L.rows ? g : L.rows - 1;  // MMA columns past the job's tokens are computed and discarded
-    int st = 0, useq = 0, k = 0;
+    const bool wr = t < L.rl / 8;  // this lane's columns are read by the epilogue
+    int st = 0, f = 0, k = 0, cur = 0;
     uint32_t sphase = 0;
-    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
-    float a2[4] = {0.f, 0.f, 0.f, 0.f}, a3[4] = {0.f, 0.f, 0.f, 0.f};
-    auto flush = [&]() {  // deposit this warp's partial of unit `useq` and start the next unit
-      const int slot = useq % NSLOT;
-      if (useq >= NSLOT) mbar_wait(cb.slot_free + slot, ((useq / NSLOT) + 1) & 1, p.timeout_ns, status);
-      *reinterpret_cast<float4*>(red + slot * SK_SLOT_FLOATS + (warp * 32 + lane) * 4) =
-          make_float4(a0[0] + a2[0] + (a1[0] + a3[0]), a0[1] + a2[1] + (a1[1] + a3[1]),
-                      a0[2] + a2[2] + (a1[2] + a3[2]), a0[3] + a2[3] + (a1[3] + a3[3]));
+    bool pend = false;
+    int fpend = 0;
+    float psc0 = 1.f, psc1 = 1.f;
+    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};  // set 0 (two chains)
+    float b0[4] = {0.f, 0.f, 0.f, 0.f}, b1[4] = {0.f, 0.f, 0.f, 0.f};  // set 1
+    auto deposit = [&](float* c0, float* c1) {  // write a finished set into its slot and clear it
+      const int slot = fpend % SK_NSLOT;
+      TRACE_T0(t_sf);
+      if (fpend >= SK_NSLOT) mbar_wait(cb.slot_free + slot, ((fpend / SK_NSLOT) + 1) & 1, p.timeout_ns, status);
+      if (warp == 0 && lane == 0) {
+        TRACE_SPAN(14, t_sf);
+        TRACE_ADD(18, 1);
+      }
+      if (wr)
+        *reinterpret_cast<float4*>(red + slot * (L.red_slot / 4) + (warp * L.rl + t * 8 + g) * 4) =
+            make_float4((c0[0] + c1[0]) * psc0, (c0[1] + c1[1]) * psc1, (c0[2] + c1[2]) * psc0, (c0[3] + c1[3]) * psc1);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) c0[i] = c1[i] = 0.f;
       __syncwarp();
       if (lane == 0) mbar_arrive(cb.slot_full + slot);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) a0[i] = a1[i] = a2[i] = a3[i] = 0.f;
-      ++useq;
+      pend = false;
     };
     for (int s = 0; s < nseg; ++s) {
       int ph, job;
@@ -579,54 +771,72 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
       segs.at(s, ph, job, u0, u1);
       if (u1 <= u0) continue;
       const int b = k % NBUF;
-      const int spu = ph ? nSB : nSA, gs = ph ? gsB : gsA, ss = ph ? ssB : ssA;
-      const int pitch = (ph ? p.I : p.H) * 2 + 16;
-      const long long nsl = (u1 - u0) * spu;
+      const int U = ph ? UB : UA, PER = ph ? L.perB : L.perA, SS = 16 * PER;
+      const int nsl = (int)(u1 - u0) * U;
+      const int nst = (nsl + SS - 1) / SS;
+      const int spe = U >= SS ? U / SS : 1;  // stages per flush event
+      const int4 jb = jobs[job];
+      const int ntok = min(jb.z, L.rows);
+      TRACE_T0(t_x);
       mbar_wait(cb.act_full + b, (k / NBUF) & 1, p.timeout_ns, status);
-      const uint8_t* xrow = bufs + (size_t)b * L.rows * L.pitch + grow * pitch;
-      // per-warp constants of the segment: where each of its stage slices sits (group offset, slice in group)
-      int goff[SK_PER], gsl[SK_PER];
-#pragma unroll
-      for (int j = 0; j < SK_PER; ++j) {
-        const int i = warp + j * SK_NW, q = i / gs;
-        goff[j] = q * gs * SK_SLICE_BYTES;
-        gsl[j] = i - q * gs;
+      if (warp == 0 && lane == 0) {
+        TRACE_SPAN(12, t_x);
+        if (ph == 1) TRACE_ONCE(10);
       }
-      const int nsl32 = (int)nsl;
-      int ucur = 0, uend = spu;  // unit this warp is accumulating, and the segment slice where it ends
-      for (int base = 0; base < nsl32; base += ss) {
+      const uint8_t* xrow = bufs + (size_t)b * L.rows * L.pitch + (size_t)(g < ntok ? g : 0) * L.pitch;
+      // column scales 2^e of this lane's tokens 2t, 2t + 1 (rows past the job's tokens are discarded)
+      const float sc0 = __uint_as_float((uint32_t)(127 + cb.xexp[b][min(2 * t, ntok - 1)]) << 23);
+      const float sc1 = __uint_as_float((uint32_t)(127 + cb.xexp[b][min(2 * t + 1, ntok - 1)]) << 23);
+      for (int i = 0; i < nst; ++i) {
+        TRACE_T0(t_f);
         mbar_wait(cb.full + st, sphase, p.timeout_ns, status);
-        const uint8_t* stage = ring + (size_t)st * L.stage_slices * SK_SLICE_BYTES;
-        const int ns = min(ss, nsl32 - base);
-#pragma unroll
-        for (int j = 0; j < SK_PER; ++j) {
-          const int i = warp + j * SK_NW;
-          if (i < ns) {
-            const int gi = base + i;
-            while (gi >= uend) {
-              flush();
-              ++ucur;
-              uend += spu;
-            }
-            if (j & 1)
-              sk_slice(stage + goff[j], gs, gsl[j], xrow, gi - (uend - spu), lane, t, a2, a3);
-            else
-              sk_slice(stage + goff[j], gs, gsl[j], xrow, gi - (uend - spu), lane, t, a0, a1);
+        TRACE_T0(t_it);
+        if (warp == 0 && lane == 0) {
+          TRACE_SPAN(ph ? 30 : 11, t_f);
+          TRACE_ONCE(9);
+        }
+        const int my0 = i * SS + warp * PER;
+        if (my0 < nsl) {
+          const uint8_t* sl = ring + (size_t)st * L.slot_bytes + (size_t)warp * PER * SK_SLICE;
+          const uint8_t* xs = xrow + (size_t)(my0 % U) * 128;
+          TRACE_T0(t_c);
+          if (cur)
+            sk_run_per(PER, sl, xs, lane, t, b0, b1);
+          else
+            sk_run_per(PER, sl, xs, lane, t, a0, a1);
+          if (warp == 0) {
+            __syncwarp();
+            if (lane == 0) TRACE_SPAN(ph ? 31 : 23, t_c);
           }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(cb.empty + st);
+        if (warp == 0 && lane == 0) TRACE_ADD(19, 1);
         if (++st == NST) {
           st = 0;
           sphase ^= 1;
         }
-      }
-      while (ucur < (int)(u1 - u0)) {
-        flush();
-        ++ucur;
+        if (pend) {
+          TRACE_T0(t_d);
+          if (cur) deposit(a0, a1); else deposit(b0, b1);
+          if (warp == 0 && lane == 0) TRACE_SPAN(25, t_d);
+        }
+        if ((i + 1) % spe == 0) {
+          pend = true;
+          fpend = f++;
+          psc0 = sc0;
+          psc1 = sc1;
+          cur ^= 1;
+        }
+        if (warp == 0 && lane == 0) TRACE_SPAN(ph ? 29 : 28, t_it);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(cb.act_empty + b);
+      // the segment's last set is written now, not after the next segment's first stage: the next segment's
+      // activations may wait (phase B) on phase-A counters that this very set completes
+      if (pend) {
+        if (cur) deposit(a0, a1); else deposit(b0, b1);
+      }
       ++k;
     }
   }
@@ -709,7 +919,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
       if (p.small_route) {
         for (int j = 0; j < njobs; ++j) p.doneA[j] = 0;
         if (p.post_norm)
-          for (int q = 0; q < rt.nroutes; ++q) p.ss[q] = 0.f;
+          for (int q = 0; q < cb.nroutes; ++q) p.ss[q] = 0.f;
       }
       p.ctl[kCtlGridArrive] = 0;
       p.ctl[kCtlExit] = 0;
@@ -728,35 +938,41 @@ extern "C" int xcb_trace_clear() {
 }
 #endif
 
-int skinny_config(int* grid_out, int* smem_out, int H, int I, int job_tokens, int small_route) {
+int skinny_config(int* grid_out, int* smem_out, int H, int I, int job_tokens, int route_R) {
   static int cached_dev = -1, cached_sms = 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return XCB_ERR_CUDA;
-  const SkLayout L = sk_layout(H, I, job_tokens, small_route);
-  if (L.nstage < 4) return XCB_ERR_UNSUPPORTED;
+  const SkLayout L = sk_layout(H, I, job_tokens, route_R);
+  if (L.nstage < 3) return XCB_ERR_UNSUPPORTED;
   if (cudaFuncSetAttribute(skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) != cudaSuccess)
     return XCB_ERR_CUDA;
   if (dev != cached_dev) {
     if (cudaDeviceGetAttribute(&cached_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return XCB_ERR_CUDA;
     cached_dev = dev;
   }
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, skinny_kernel, SK_THREADS, L.total) != cudaSuccess ||
-      per_sm < 1)
-    return XCB_ERR_CUDA;
-  *grid_out = cached_sms * per_sm;
+  *grid_out = cached_sms;  // one CTA per SM (the kernel takes nearly all shared memory)
   *smem_out = L.total;
   return XCB_OK;
 }
 
-size_t skinny_smem_bytes(int H, int I) {
-  const SkLayout L = sk_layout(H, I, kJobTokens, 1);
-  return L.nstage >= 4 ? (size_t)L.total : (size_t)1 << 30;
+// Tokens per job for the in-kernel router: the most (up to `want`) whose shared-memory plan keeps the stage sizes
+// of the one-token plan, so that batches of a few tokens do not fall back to small copies.
+int skinny_job_cap(int H, int I, int want, int route_R) {
+  const SkLayout one = sk_layout(H, I, 1, route_R);
+  for (int r = want < kJobTokens ? want : kJobTokens; r > 1; --r) {
+    const SkLayout L = sk_layout(H, I, r, route_R);
+    if (L.nstage >= 3 && L.perA == one.perA && L.perB == one.perB) return r;
+  }
+  return 1;
+}
+
+bool skinny_supported(int H, int I) {
+  return sk_layout(H, I, kJobTokens, kSmallRoutes).nstage >= 3 && sk_layout(H, I, 1, kSmallRoutes).nstage >= 3;
 }
 
 int launch_skinny(const SkinnyParams& p, cudaStream_t stream) {
   int grid = 0, smem = 0;
-  int rc = skinny_config(&grid, &smem, p.H, p.I, p.job_tokens, p.small_route);
+  int rc = skinny_config(&grid, &smem, p.H, p.I, p.job_tokens, p.small_route ? p.T * p.k : 0);
   if (rc != XCB_OK) return rc;
   skinny_kernel<<<grid, SK_THREADS, smem, stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;

@@ -5,33 +5,23 @@ Replaces the reference's host-side repack (kernels/moe_w4a16_h200/moe_w4a16.py:3
 the layout constants; the bytes themselves are produced on the GPU by ``xcb_moe_pack_weights`` in the C-ABI
 library, which reads the four 256-entry XOR tables built below.
 
-Decode-path ("skinny") layout of one expert matrix W [R rows, K] (K % 256 == 0, R % 16 == 0):
+Decode-path ("skinny") layout of one expert matrix W [R rows, K] (K % 256 == 0, R % 16 == 0).  It feeds the
+hardware FP4 converter of sm_100a (``cvt.rn.f16x2.e2m1x2``: one code byte -> two f16, low nibble first) and the
+m16n8k16 tensor-core step, so it is a pure byte permutation of the reference tensors (no transform, no folding):
 
 * Rows are taken in *packed order*: for gate_up, 16-row block ``rb`` holds gate rows 8rb..8rb+7 then up rows
   8rb..8rb+7 (so one mma.sync accumulator lane owns the gate and the up value of the same intermediate
   feature); for down, rows stay in order.
-* A block is one *unit* of ``9*K`` bytes, cut into equal groups of ``gs = group_slices(K)`` slices (64 k each;
-  16 when K/64 is a multiple of 16, else 12, 8 or 4); a group holds its codes ``[gs slices][32 lanes][4 steps]``
-  u32 (``gs * 512`` bytes) followed by its scale codes ``[gs/4][32 lanes][4 slices][2 row halves]`` bytes
-  (``gs * 64``).  Consecutive units of one expert are contiguous, so the kernel streams any run of them as
-  fixed-size bulk copies of whole groups.
-* Lane L = 4g + t, slice S, step j holds the 8 codes of rows {g, g+8} at k = 64S + 16t + 4j + {0,1,2,3}.
-  All 16 k of a lane's slice share one 16-wide scale block (4S + t), so one scale pair serves four steps.
-  The activation operand of that step is x[token][64S + 16t + 4j + 0..3]: 16 consecutive k per lane and slice.
-* The natural word (bytes: W[g][k/2], W[g+8][k/2], W[g][k/2+1], W[g+8][k/2+1]; low nibble = even k) is stored
-  as ``T(word)`` with ``T = D^-1 P``: ``P`` sends nibble n to the bf16 fields (sign 15, exponent 8..7,
-  mantissa 6, +16 for the high half) of register n // 2, half n % 2; ``D`` is the decoder the kernel runs:
-
-      r0 = q & M;   r1 = (q << 4) & M;   r2 = ((q << 6) ^ rotl(q, 10)) & M;   r3 = ((q << 6) ^ rotl(q, 12)) & M
-
-  with M = 0x81C081C0.  Each register then holds two bf16 values e2m1 * 2^-126.  The four shift sources are the
-  minimum for this mask: the mask repeats with period 16 so no three shifts, rotations or byte permutations
-  of q cover all 32 input bits (checked by ``decoder_search``).
-* Scale bytes are canonicalised losslessly at pack time: a zero scale zeroes its 16 codes, a negative scale
-  flips its codes' sign bits, and the magnitude is re-encoded as ``c = ((E + 9) << 3) | m`` for the value
-  ``2^E (1 + m/8)``, E in [-9, 8] (the E4M3 subnormals become normal).  The kernel forms the bf16 factor
-  ``(c << 4) | 0x6000`` = value * 2^74 with one integer multiply-add; the decoded weight in bf16 is
-  exactly ``e2m1 * sf * 2^-52`` and the epilogue multiplies by ``gs * 2^52``.
+* A block is one *unit* of ``9*K`` bytes: K/64 slice records of 576 bytes, each ``[32 lanes][4 steps]`` u32 of
+  codes (512 bytes) followed by ``[32 lanes][2 row halves]`` scale bytes (64).  Consecutive units of one expert
+  are contiguous, so the kernel streams any run of them as bulk copies of whole slices.
+* Lane L = 4g + t, slice S, step j holds the word (W[g][b], W[g+8][b], W[g][b+1], W[g+8][b+1]) of code bytes
+  b = 32S + 8t + 2j (low nibble = even k): the four f16x2 A-fragment registers of rows {g, g+8} at
+  k = 64S + 16t + 4j + {0,1,2,3}.  All 16 k of a lane's slice share one 16-wide scale block (4S + t), so one
+  scale pair serves four steps; the activation operand of that step is x[token][64S + 16t + 4j + 0..3].
+* The lane's two scale bytes are the raw E4M3 scales of rows g and g + 8 for block 4S + t (converted to f16x2 by
+  ``cvt.rn.f16x2.e4m3x2``).  Each f16 weight e2m1 * e4m3 is exact (at most 6 significant bits, magnitude in
+  [2^-10, 2688]); the epilogue multiplies by the fp32 global scale.
 
 Prefill-path ("wide") layout of the same matrix, stored after the decode-path bytes in the same buffer.  It feeds
 the tcgen05 kernel, whose dequantising threads write one weight row each into a tensor-memory lane (the MMA's A
@@ -44,8 +34,20 @@ operand), so a word holds 8 consecutive k of ONE row:
   its codes ``[2 halves][128 rows][4 words]`` u32 (4096 bytes; half j, word w cover k = 64c + 32j + 8w .. +7) then
   its scale codes ``[128 rows][4 blocks]`` bytes (512).  The blocks of one expert are consecutive.
 * The natural word is the row's 4 code bytes at k/2 (low nibble = even k), so the decoder's register i holds
-  (k + 2i, k + 2i + 1), exactly a tensor-memory column of two bf16; it is stored as ``T(word)`` with the same T
-  and the same scale canonicalisation as the decode-path layout.
+  (k + 2i, k + 2i + 1), exactly a tensor-memory column of two bf16; it is stored as ``T(word)`` with ``T = D^-1 P``:
+  ``P`` sends nibble n to the bf16 fields (sign 15, exponent 8..7, mantissa 6, +16 for the high half) of register
+  n // 2, half n % 2; ``D`` is the decoder the kernel runs:
+
+      r0 = q & M;   r1 = (q << 4) & M;   r2 = ((q << 6) ^ rotl(q, 10)) & M;   r3 = ((q << 6) ^ rotl(q, 12)) & M
+
+  with M = 0x81C081C0.  Each register then holds two bf16 values e2m1 * 2^-126.  The four shift sources are the
+  minimum for this mask: the mask repeats with period 16 so no three shifts, rotations or byte permutations
+  of q cover all 32 input bits (checked by ``decoder_search``).
+* Scale bytes are canonicalised losslessly at pack time: a zero scale zeroes its 16 codes, a negative scale
+  flips its codes' sign bits, and the magnitude is re-encoded as ``c = ((E + 9) << 3) | m`` for the value
+  ``2^E (1 + m/8)``, E in [-9, 8] (the E4M3 subnormals become normal).  The kernel forms the bf16 factor
+  ``(c << 4) | 0x6000`` = value * 2^74 with one integer multiply-add; the decoded weight in bf16 is
+  exactly ``e2m1 * sf * 2^-52`` and the epilogue multiplies by ``gs * 2^52``.
 """
 from __future__ import annotations
 
@@ -180,12 +182,6 @@ def scale_code_value(c: int) -> float:
 
 
 # --------------------------------------------------------------------------------------------- sizes
-def group_slices(K: int) -> int:
-    """Slices per group for reduction length K (mirrors group_slices in the CUDA sources)."""
-    n = K // 64
-    return 16 if n % 16 == 0 else 12 if n % 12 == 0 else 8 if n % 8 == 0 else 4
-
-
 def unit_bytes(K: int) -> int:
     return 9 * K
 
