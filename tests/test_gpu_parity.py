@@ -312,3 +312,28 @@ def test_repeated_expert_within_a_token(dev):
     out = layer.forward(xd, None, topk_ids=torch.from_numpy(ids).to(dev), topk_weights=torch.from_numpy(wts).to(dev))
     torch.cuda.synchronize()
     assert_close_bf16(out, oracle_layer(xd, weights, ids, wts))
+
+
+@pytest.mark.parametrize("T,path", [(1, "decode"), (3, "decode"), (3, "prefill")])
+def test_activations_beyond_f16_range(dev, T, path):
+    """Activations far outside the f16 range (|x| up to ~1e7) and tiny ones in the same rows: the decode kernel
+    converts each token's row to f16 with a power-of-two scale, so the output must still match the oracle."""
+    from xcalibur_b200 import PreparedMoE
+
+    rng = np.random.default_rng(60 + T)
+    E, H, I, k = 8, 1024, 512, 2
+    w = moe_ref.make_weights(rng, E, H, I)
+    weights = _weights_from_np(w, dev)
+    layer = PreparedMoE(*weights.values())
+    x, logits = moe_ref.make_inputs(rng, T, H, E)
+    xf = moe_ref.bf16_bits_to_f32(x) * np.float32(3.0e6)
+    xf[:, ::7] *= np.float32(1e-12)                      # tiny values beside the large ones
+    xd = torch.from_numpy(xf).to(dev).to(torch.bfloat16)
+    out, ids, wts = layer.forward(xd, torch.from_numpy(logits).to(dev), k, return_routing=True, path=path)
+    torch.cuda.synchronize()
+    assert layer.check_device_status() == 0
+    ref = moe_ref.bf16_bits_to_f32(oracle_layer(xd, weights, to_np(ids), to_np(wts)))
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    scale = np.abs(ref).max()
+    assert np.abs(got - ref).max() <= 1e-2 * scale

@@ -187,16 +187,19 @@ __device__ __forceinline__ float key_float(uint32_t k) {
 
 // Top-k of one token's logits by one warp: rank by value descending, ties to the lower index; weights = softmax
 // over the selected logits (summed in route order).  Lane s < k returns route s in (id, w).  E <= 512.
-// Each round is two warp reductions: the largest key, then the lowest index holding it.
-__device__ __forceinline__ void warp_topk(const float* row, int E, int k, int& id, float& w) {
+// Each round is two warp reductions: the largest key, then the lowest index holding it.  The first half loads the
+// row into registers (split out so a caller can issue the loads early).
+__device__ __forceinline__ void warp_topk_load(const float* row, int E, uint32_t (&key)[16]) {
   const int lane = threadIdx.x & 31;
   const int per = (E + 31) / 32;
-  uint32_t key[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const int e = lane + 32 * j;
     key[j] = (j < per && e < E) ? float_key(row[e]) : 0u;  // 0 is below every real key
   }
+}
+__device__ __forceinline__ void warp_topk_select(const uint32_t (&key)[16], int k, int& id, float& w) {
+  const int lane = threadIdx.x & 31;
   uint32_t used = 0, my_key = 0;
   int my_i = -1;
   for (int s = 0; s < k; ++s) {
@@ -222,6 +225,11 @@ __device__ __forceinline__ void warp_topk(const float* row, int E, int k, int& i
   for (int s = 0; s < k; ++s) den += __shfl_sync(0xffffffffu, ex, s);
   id = my_i;
   w = ex / den;
+}
+__device__ __forceinline__ void warp_topk(const float* row, int E, int k, int& id, float& w) {
+  uint32_t key[16];
+  warp_topk_load(row, E, key);
+  warp_topk_select(key, k, id, w);
 }
 
 }  // namespace xcb

@@ -20,11 +20,11 @@
 // * Partial sums leave the compute warps only at stage ends: each warp accumulates into one of two register
 //   sets, switches set at every flush point, and writes the finished set one stage later (its MMAs have long
 //   completed) or at the end of its segment, into a reduction slot.  Two epilogue warps consume the slots in order: they add the partials
-//   of each unit in warp order (deterministic), apply the epilogue (SwiGLU -> inter, or y and the post-norm
-//   sums) and hand finished units to the signalling warp.
+//   of each unit in warp order (deterministic) and apply the epilogue (SwiGLU -> inter, or y and the post-norm
+//   sums).
 // * Warp 17 stages each segment's activation rows (x for phase A, the job's SwiGLU output for phase B, after an
-//   acquire on that job's phase-A counter) with bulk copies and converts them to f16 in place; warp 18 publishes
-//   finished work GPU-wide (one fence and one counter update per segment).
+//   acquire on that job's phase-A counter) with bulk copies and converts them to f16 in place; the epilogue warp
+//   that finishes a segment's last unit publishes it GPU-wide (one fence and one counter update per segment).
 // * Combine: the CTA whose phase-B units complete a 16-row block forms out = bf16(sum_s w_s * y_s) for it; with the
 //   post-norm, or for large batches, a bounded grid barrier precedes a combine spread over all CTAs.
 // * Small batches (T*k <= 256) route inside the kernel (every CTA computes the same tables; up to 32 routes with
@@ -66,10 +66,9 @@ __device__ unsigned long long g_trace[1024 * kTraceSlots];
 constexpr int SK_NW = 16;                               // compute warps
 constexpr int SK_W_PROD = SK_NW;                        // weight producer warp
 constexpr int SK_W_ACT = SK_NW + 1;                     // activation staging warp
-constexpr int SK_W_SIG = SK_NW + 2;                     // signalling warp
-constexpr int SK_W_EPI = SK_NW + 3;                     // reduction + epilogue warps (SK_NEPI of them)
+constexpr int SK_W_EPI = SK_NW + 2;                     // reduction + epilogue warps (SK_NEPI of them)
 constexpr int SK_NEPI = 2;                              // epilogue warp e takes the flush events f with f % 2 == e
-constexpr int SK_THREADS = (SK_NW + 3 + SK_NEPI) * 32;
+constexpr int SK_THREADS = (SK_NW + 2 + SK_NEPI) * 32;  // 20 warps: at most 5 per SM sub-partition
 constexpr int SK_SLICE = 576;                           // 512 B of codes + 64 B of scale bytes per 64-k slice
 constexpr int SK_PER_MAX = 7;                           // slices per compute warp per stage
 constexpr int SK_MAX_STAGES = 8;
@@ -84,22 +83,90 @@ constexpr int SK_SMEM_LIMIT = 227 * 1024;
 // Slices per warp per stage for a unit of U slices: U % PER == 0 (a warp's slices never straddle a unit) and
 // either U % (16 PER) == 0 (a unit spans whole stages) or (16 PER) % U == 0 (a stage holds whole units).
 __host__ __device__ inline int sk_per(int U, int per_max) {
-  for (int per = per_max; per >= 1; --per)
+  for (int per = per_max; per >= 1; --per) {
+    if (per == 5 || per == 3) continue;  // not instantiated (sk_run_per): fewer copies of the hot loop
     if (U % per == 0 && ((16 * per) % U == 0 || U % (16 * per) == 0)) return per;
+  }
   return 0;
 }
+
+// The units of one CTA, cut into segments of one job and one phase, in processing order.  The jobs are split into
+// two waves (first and second half of the job list) and the work runs as four sequences: gate_up of wave 0,
+// gate_up of wave 1, down of wave 0, down of wave 1; every CTA takes a contiguous share of each sequence.  The
+// down projection of a wave thus depends on gate_up work that finished one sequence earlier on every CTA, so the
+// phase A -> B handoff costs no wait.  A unit is numbered job * nrb + rb within its phase.
+struct SkSegments {
+  // per sequence q (as scalars, so no array is indexed at run time): unit range, first job, jobs touched
+  long long u0_0, u0_1, u0_2, u0_3, u1_0, u1_1, u1_2, u1_3;
+  int jf_0, jf_1, jf_2, jf_3, nj_0, nj_1, nj_2, nj_3;
+  int nrbA, nrbB;
+
+  template <typename T>
+  __device__ static T pick(int q, T a, T b, T c, T d) { return q == 0 ? a : (q == 1 ? b : (q == 2 ? c : d)); }
+
+  __device__ void init(int njobs, int nA_rb, int nB_rb, int G, int bid) {
+    nrbA = nA_rb;
+    nrbB = nB_rb;
+    const int W = njobs >= 2 ? 2 : 1;
+    long long a[4], b[4];
+    int f[4], n[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int ph = q >> 1, w = q & 1;
+      const int nrb = ph ? nrbB : nrbA;
+      const int j0 = w < W ? njobs * w / W : njobs, j1 = w < W ? njobs * (w + 1) / W : njobs;
+      const long long cnt = (long long)(j1 - j0) * nrb;
+      a[q] = (long long)j0 * nrb + cnt * bid / G;
+      b[q] = (long long)j0 * nrb + cnt * (bid + 1) / G;
+      f[q] = (int)(a[q] / nrb);
+      n[q] = b[q] > a[q] ? (int)((b[q] - 1) / nrb) - f[q] + 1 : 0;
+    }
+    u0_0 = a[0]; u0_1 = a[1]; u0_2 = a[2]; u0_3 = a[3];
+    u1_0 = b[0]; u1_1 = b[1]; u1_2 = b[2]; u1_3 = b[3];
+    jf_0 = f[0]; jf_1 = f[1]; jf_2 = f[2]; jf_3 = f[3];
+    nj_0 = n[0]; nj_1 = n[1]; nj_2 = n[2]; nj_3 = n[3];
+  }
+  __device__ int count() const { return nj_0 + nj_1 + nj_2 + nj_3; }
+  __device__ int first_b() const { return nj_0 + nj_1; }  // index of the first phase-B segment
+  __device__ long long units_a() const { return u1_0 - u0_0 + u1_1 - u0_1; }
+  __device__ long long units_b() const { return u1_2 - u0_2 + u1_3 - u0_3; }
+  // Segment i: phase, job, unit range [v0, v1).
+  __device__ void at(int i, int& ph, int& job, long long& v0, long long& v1) const {
+    int q = 0;
+    if (i >= nj_0) {
+      i -= nj_0;
+      q = 1;
+      if (i >= nj_1) {
+        i -= nj_1;
+        q = 2;
+        if (i >= nj_2) {
+          i -= nj_2;
+          q = 3;
+        }
+      }
+    }
+    ph = q >> 1;
+    job = pick(q, jf_0, jf_1, jf_2, jf_3) + i;
+    const long long nrb = ph ? nrbB : nrbA;
+    const long long a = pick(q, u0_0, u0_1, u0_2, u0_3), b = pick(q, u1_0, u1_1, u1_2, u1_3);
+    v0 = a > job * nrb ? a : job * nrb;
+    v1 = b < (job + 1) * nrb ? b : (job + 1) * nrb;
+  }
+};
 
 // Control block: mbarriers and bookkeeping.
 struct SkCtl {
   uint64_t full[SK_MAX_STAGES], empty[SK_MAX_STAGES];
   uint64_t act_land[SK_NBUF_MAX], act_full[SK_NBUF_MAX], act_empty[SK_NBUF_MAX];
   uint64_t slot_full[SK_NSLOT], slot_free[SK_NSLOT];
-  int seg_cnt[SK_SEG_RING];
-  int seg_gen[SK_SEG_RING];
+  uint64_t x_land;                    // one-token calls: the token's row, copied at kernel start
+  int xpart[SK_NW];                   // per-warp partial maxima of that row's conversion
+  int seg_cnt[SK_SEG_RING];           // units of segment k finished (slot k % SK_SEG_RING)
   int xexp[SK_NBUF_MAX][kJobTokens];  // per activation buffer and row: x was multiplied by 2^-xexp
   int list[512];                      // 16-row blocks this CTA completed (H <= 8192)
   int nlist;
   int njobs, nroutes;
+  SkSegments segs;                    // written once by thread 0, read by every role (keeps it out of registers)
 };
 
 struct SkLayout {
@@ -158,44 +225,6 @@ struct SkTables {
         order(reinterpret_cast<int*>(base + cap * 28)) {}
 };
 
-// The units of one CTA, cut into segments of one job and one phase, in processing order: a contiguous share of
-// all phase-A units, then a contiguous share of all phase-B units.
-struct SkSegments {
-  int njobs, nrbA, nrbB;
-  long long a0, a1, b0, b1;  // this CTA's unit ranges
-  int jA0, nAj, jB0, nBj;    // jobs the ranges touch
-
-  __device__ void init(int nj, int nA_rb, int nB_rb, int G, int bid) {
-    njobs = nj;
-    nrbA = nA_rb;
-    nrbB = nB_rb;
-    const long long nA = (long long)njobs * nrbA, nB = (long long)njobs * nrbB;
-    a0 = nA * bid / G;
-    a1 = nA * (bid + 1) / G;
-    b0 = nB * bid / G;
-    b1 = nB * (bid + 1) / G;
-    jA0 = (int)(a0 / nrbA);
-    nAj = a1 > a0 ? (int)((a1 - 1) / nrbA) - jA0 + 1 : 0;
-    jB0 = (int)(b0 / nrbB);
-    nBj = b1 > b0 ? (int)((b1 - 1) / nrbB) - jB0 + 1 : 0;
-  }
-  __device__ int count() const { return nAj + nBj; }
-  // Segment i: phase, job, unit range [u0, u1) in the phase's unit numbering (job * nrb + rb).
-  __device__ void at(int i, int& ph, int& job, long long& u0, long long& u1) const {
-    if (i < nAj) {
-      ph = 0;
-      job = jA0 + i;
-      u0 = a0 > (long long)job * nrbA ? a0 : (long long)job * nrbA;
-      u1 = a1 < (long long)(job + 1) * nrbA ? a1 : (long long)(job + 1) * nrbA;
-    } else {
-      ph = 1;
-      job = jB0 + i - nAj;
-      u0 = b0 > (long long)job * nrbB ? b0 : (long long)job * nrbB;
-      u1 = b1 < (long long)(job + 1) * nrbB ? b1 : (long long)(job + 1) * nrbB;
-    }
-  }
-};
-
 // ------------------------------------------------------------------------------------------------ arithmetic
 __device__ __forceinline__ void cvt_e2m1x8(uint32_t q, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
@@ -227,8 +256,9 @@ __device__ __forceinline__ uint32_t h2mul_hi(uint32_t a, uint32_t s) {  // a * (
 
 // One 64-k slice of one unit for one warp: lane (g, t) holds the codes of rows g and g + 8 at k = 16t + 4i + 0..3
 // of the slice for step i, and the scale pair of block t; xs = the f16 activation row at the slice's first k.
-__device__ __forceinline__ void sk_slice(const uint8_t* sl, const uint8_t* xs, int lane, int t, float* acc0,
-                                         float* acc1) {
+// Steps alternate between the set's two chains.  (Four chains would need more than the 80 registers a thread
+// may hold when six warps of this CTA share one SM sub-partition.)
+__device__ __forceinline__ void sk_slice(const uint8_t* sl, const uint8_t* xs, int lane, int t, float (&c)[2][4]) {
   const uint4 cw = *reinterpret_cast<const uint4*>(sl + lane * 16);
   const uint32_t sc = *reinterpret_cast<const uint16_t*>(sl + 512 + lane * 2);
   const uint4 xa = *reinterpret_cast<const uint4*>(xs + t * 32);
@@ -236,31 +266,29 @@ __device__ __forceinline__ void sk_slice(const uint8_t* sl, const uint8_t* xs, i
   const uint32_t s2 = cvt_e4m3x2(sc);
   uint32_t r0, r1, r2, r3;
   cvt_e2m1x8(cw.x, r0, r1, r2, r3);
-  mma_16816_f16(acc0, h2mul_lo(r0, s2), h2mul_hi(r1, s2), h2mul_lo(r2, s2), h2mul_hi(r3, s2), xa.x, xa.y);
+  mma_16816_f16(c[0], h2mul_lo(r0, s2), h2mul_hi(r1, s2), h2mul_lo(r2, s2), h2mul_hi(r3, s2), xa.x, xa.y);
   cvt_e2m1x8(cw.y, r0, r1, r2, r3);
-  mma_16816_f16(acc1, h2mul_lo(r0, s2), h2mul_hi(r1, s2), h2mul_lo(r2, s2), h2mul_hi(r3, s2), xa.z, xa.w);
+  mma_16816_f16(c[1], h2mul_lo(r0, s2), h2mul_hi(r1, s2), h2mul_lo(r2, s2), h2mul_hi(r3, s2), xa.z, xa.w);
   cvt_e2m1x8(cw.z, r0, r1, r2, r3);
-  mma_16816_f16(acc0, h2mul_lo(r0, s2), h2mul_hi(r1, s2), h2mul_lo(r2, s2), h2mul_hi(r3, s2), xb.x, xb.y);
+  mma_16816_f16(c[0], h2mul_lo(r0, s2), h2mul_hi(r1, s2), h2mul_lo(r2, s2), h2mul_hi(r3, s2), xb.x, xb.y);
   cvt_e2m1x8(cw.w, r0, r1, r2, r3);
-  mma_16816_f16(acc1, h2mul_lo(r0, s2), h2mul_hi(r1, s2), h2mul_lo(r2, s2), h2mul_hi(r3, s2), xb.z, xb.w);
+  mma_16816_f16(c[1], h2mul_lo(r0, s2), h2mul_hi(r1, s2), h2mul_lo(r2, s2), h2mul_hi(r3, s2), xb.z, xb.w);
 }
 
-// PER consecutive slices of one warp into one accumulator pair (compile-time PER so the slices interleave).
+// PER consecutive slices of one warp into one accumulator set (compile-time PER so the slices interleave).
 template <int PER>
-__device__ __forceinline__ void sk_run(const uint8_t* sl, const uint8_t* xs, int lane, int t, float* acc0, float* acc1) {
+__device__ __forceinline__ void sk_run(const uint8_t* sl, const uint8_t* xs, int lane, int t, float (&c)[2][4]) {
 #pragma unroll
-  for (int j = 0; j < PER; ++j) sk_slice(sl + j * SK_SLICE, xs + j * 128, lane, t, acc0, acc1);
+  for (int j = 0; j < PER; ++j) sk_slice(sl + j * SK_SLICE, xs + j * 128, lane, t, c);
 }
-__device__ __forceinline__ void sk_run_per(int per, const uint8_t* sl, const uint8_t* xs, int lane, int t, float* a0,
-                                           float* a1) {
-  switch (per) {
-    case 7: sk_run<7>(sl, xs, lane, t, a0, a1); break;
-    case 6: sk_run<6>(sl, xs, lane, t, a0, a1); break;
-    case 5: sk_run<5>(sl, xs, lane, t, a0, a1); break;
-    case 4: sk_run<4>(sl, xs, lane, t, a0, a1); break;
-    case 3: sk_run<3>(sl, xs, lane, t, a0, a1); break;
-    case 2: sk_run<2>(sl, xs, lane, t, a0, a1); break;
-    default: sk_run<1>(sl, xs, lane, t, a0, a1); break;
+__device__ __forceinline__ void sk_run_per(int per, const uint8_t* sl, const uint8_t* xs, int lane, int t,
+                                           float (&c)[2][4]) {
+  switch (per) {  // the slice counts sk_per can return
+    case 7: sk_run<7>(sl, xs, lane, t, c); break;
+    case 6: sk_run<6>(sl, xs, lane, t, c); break;
+    case 4: sk_run<4>(sl, xs, lane, t, c); break;
+    case 2: sk_run<2>(sl, xs, lane, t, c); break;
+    default: sk_run<1>(sl, xs, lane, t, c); break;
   }
 }
 
@@ -372,8 +400,13 @@ __device__ void sk_route_small(const SkinnyParams& p, SkTables& rt, SkCtl& cb, i
       for (int s0 = 0; s0 < c; s0 += JC, ++j) rt.jobs[j] = make_int4(e, offs[e] + s0, min(JC, c - s0), 0);
     }
   }
-  __syncthreads();
-  if (blockIdx.x == 0) {  // publish the routing (tests and callers read it from the workspace)
+}
+
+// CTA 0 publishes the routing tables to the workspace (tests and callers read them there); all its threads.
+__device__ void sk_publish(const SkinnyParams& p, const SkTables& rt, const SkCtl& cb) {
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int R = p.T * p.k;
+  {
     for (int f = tid; f < R; f += nthr) {
       p.g_ids[f] = rt.ids[f];
       p.g_wts[f] = rt.wts[f];
@@ -394,6 +427,37 @@ __device__ void sk_route_small(const SkinnyParams& p, SkTables& rt, SkCtl& cb, i
       if (e < p.E_loc) p.g_counts[e] = c;
       p.g_offsets[e] = below;
     }
+  }
+}
+
+// One token with router logits (warp 0; the keys were loaded before the barrier set-up): the top-k routes name
+// distinct experts, so each local route is one job of one token, and a route's position in the expert order is the
+// number of local routes with a lower expert id.
+__device__ void sk_route_one(const SkinnyParams& p, const uint32_t (&key)[16], SkTables& rt, SkCtl& cb) {
+  const int lane = threadIdx.x & 31;
+  int id;
+  float w;
+  warp_topk_select(key, p.k, id, w);
+  const int el = id - p.lo;
+  const bool loc = lane < p.k && el >= 0 && el < p.E_loc;
+  int below = 0;
+  for (int j = 0; j < p.k; ++j) {
+    const int e2 = __shfl_sync(0xffffffffu, loc ? el : 0x7fffffff, j);
+    below += (e2 < el);
+  }
+  if (lane < p.k) {
+    rt.ids[lane] = id;
+    rt.wts[lane] = w;
+    rt.pos[lane] = loc ? below : -1;
+    if (loc) {
+      rt.order[below] = lane;
+      rt.jobs[below] = make_int4(el, below, 1, 0);
+    }
+  }
+  const int n = __popc(__ballot_sync(0xffffffffu, loc));
+  if (lane == 0) {
+    cb.njobs = n;
+    cb.nroutes = n;
   }
 }
 
@@ -431,9 +495,46 @@ __device__ void sk_rows_to_f16(uint8_t* buf, int pitch, int ntok, int K, int* xe
   }
 }
 
-__global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
+// Convert one staged bf16 row of K values to f16 in place with `nw` warps (this one is number `wid`), the same
+// power-of-two scaling as sk_rows_to_f16, writing a second copy to `copy` when it is not null; named barrier `bar`
+// joins the warps between the max pass and the conversion.  Returns the exponent e.
+__device__ int sk_row_to_f16_warps(uint8_t* row, uint8_t* copy, int K, int* part, int wid, int nw, int bar) {
+  const int lane = threadIdx.x & 31, nv = K / 8;
+  const int v0 = nv * wid / nw, v1 = nv * (wid + 1) / nw;
+  uint4* r = reinterpret_cast<uint4*>(row);
+  uint4* c = reinterpret_cast<uint4*>(copy);
+  uint32_t m = 0;
+  for (int v = v0 + lane; v < v1; v += 32) {
+    const uint4 q = r[v];
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m = max(m, max(w[i] & 0x7FFFu, (w[i] >> 16) & 0x7FFFu));
+  }
+  m = __reduce_max_sync(0xffffffffu, m);
+  if (lane == 0) part[wid] = (int)m;
+  named_bar(bar, nw * 32);
+  int mm = 0;
+  for (int i = 0; i < nw; ++i) mm = max(mm, part[i]);
+  const int E = mm >> 7;
+  const int e = E > 141 ? E - 141 : 0;
+  const float sc = __uint_as_float((uint32_t)(127 - e) << 23);
+  for (int v = v0 + lane; v < v1; v += 32) {
+    const uint4 q = r[v];
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 h = __floats2half2_rn(__uint_as_float(w[i] << 16) * sc, __uint_as_float(w[i] & 0xFFFF0000u) * sc);
+      o[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    r[v] = make_uint4(o[0], o[1], o[2], o[3]);
+    if (copy) c[v] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  return e;
+}
+
+__global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParams p, const SkLayout L) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  const SkLayout L = sk_layout(p.H, p.I, p.job_tokens, p.small_route ? p.T * p.k : 0);
   uint8_t* ring = smem + L.ring;
   uint8_t* bufs = smem + L.buf;
   float* red = reinterpret_cast<float*>(smem + L.red);
@@ -443,9 +544,23 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
   const int NST = L.nstage, NBUF = L.nbuf;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, bid = blockIdx.x;
+  // one token and one row per job (so not an expert named twice by precomputed routing): every phase-A segment
+  // uses that token's row, staged before routing into row 0 of buffers 0 and 1
+  const bool xpre = p.T == 1 && p.job_tokens == 1;
 
+  // one token with logits: warp 0 loads the row now, so the load overlaps the set-up below
+  const bool route_one = p.small_route && p.T == 1 && p.logits != nullptr;
+  uint32_t key[16];
+  if (route_one && warp == 0) warp_topk_load(p.logits, p.E_tot, key);
   if (tid == 0) {
     TRACE_AT(0);
+#if XCB_TRACE
+    {
+      uint32_t smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      g_trace[blockIdx.x * kTraceSlots + 2] = smid;
+    }
+#endif
     for (int i = 0; i < NST; ++i) {
       mbar_init(cb.full + i, 1);
       mbar_init(cb.empty + i, SK_NW);
@@ -459,17 +574,33 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
       mbar_init(cb.slot_full + i, SK_NW);
       mbar_init(cb.slot_free + i, 1);
     }
+    mbar_init(&cb.x_land, 1);
     fence_mbar_init();
     cb.nlist = 0;
+    if (xpre) {  // one token: every phase-A segment uses its row, so copy it now and convert it while routing
+      mbar_arrive_expect_tx(&cb.x_land, p.H * 2);
+      bulk_g2s(bufs, p.x, p.H * 2, &cb.x_land);
+    }
   }
-  for (int i = tid; i < SK_SEG_RING; i += SK_THREADS) {
-    cb.seg_cnt[i] = 0;
-    cb.seg_gen[i] = 0;
+  for (int i = tid; i < SK_SEG_RING; i += SK_THREADS) cb.seg_cnt[i] = 0;
+  __syncthreads();  // barrier initialisation visible to every warp
+  if (xpre && warp >= SK_NW - 12 && warp < SK_NW) {
+    // 12 compute warps convert the token's row while warp 0 (and the router) pick its experts
+    mbar_wait(&cb.x_land, 0, p.timeout_ns, status);
+    const int e = sk_row_to_f16_warps(bufs, NBUF > 1 ? bufs + (size_t)L.rows * L.pitch : nullptr, p.H, cb.xpart,
+                                      warp - (SK_NW - 12), 12, 1);
+    if (warp == SK_NW - 12 && lane == 0) {
+      cb.xexp[0][0] = e;
+      cb.xexp[1][0] = e;
+    }
   }
-  if (p.small_route) {
+  if (route_one) {
+    if (warp == 0) sk_route_one(p, key, rt, cb);
+  } else if (p.small_route) {
     sk_route_small(p, rt, cb, reinterpret_cast<int*>(ring));
   }
   __syncthreads();
+  if (p.small_route && bid == 0) sk_publish(p, rt, cb);
   if (tid == 0) TRACE_AT(1);
 
   const int njobs = p.small_route ? cb.njobs : p.ctl[kCtlJobs];
@@ -480,8 +611,9 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
   const int nrbA = (2 * p.I) / 16, nrbB = p.H / 16;
   const int UA = p.H / 64, UB = p.I / 64;  // slices per unit
   const size_t unitA = (size_t)9 * p.H, unitB = (size_t)9 * p.I;
-  SkSegments segs;
-  segs.init(njobs, nrbA, nrbB, G, bid);
+  if (tid == 0) cb.segs.init(njobs, nrbA, nrbB, G, bid);
+  __syncthreads();
+  const SkSegments& segs = cb.segs;
   const int nseg = segs.count();
 
   if (warp == SK_W_PROD) {
@@ -493,12 +625,14 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
       // phase-B weights do not depend on phase A: when they fit in L2, this CTA's share is prefetched into L2 a
       // piece per phase-A stage (so HBM sees one even stream) and phase B reads L2 after the A -> B handoff
       const bool prefetch_b = (long long)njobs * nrbB * (long long)unitB <= SK_L2_PREFETCH_BYTES;
-      int pf_seg = segs.nAj;           // next phase-B segment to prefetch
+      int pf_seg = segs.first_b();     // next phase-B segment to prefetch
       size_t pf_off = 0;               // bytes of it already prefetched
       size_t pf_step = 0;              // bytes per phase-A stage
-      if (prefetch_b && segs.nAj > 0) {
-        const long long nA = segs.a1 - segs.a0, nB = segs.b1 - segs.b0;
-        const long long stagesA = (nA * UA + 16 * L.perA - 1) / (16 * L.perA) + segs.nAj;
+      if (prefetch_b && segs.first_b() > 0) {
+        // spread over the phase-A stages after the first ring fill (the first stages land sooner without it)
+        const long long nA = segs.units_a(), nB = segs.units_b();
+        long long stagesA = (nA * UA + 16 * L.perA - 1) / (16 * L.perA) + segs.first_b() - NST;
+        stagesA = stagesA < 1 ? 1 : stagesA;
         pf_step = (size_t)((nB * (long long)unitB + stagesA - 1) / stagesA + 4095) & ~(size_t)4095;
       }
       auto prefetch_b_bytes = [&](size_t budget) {  // issue up to `budget` bytes of the remaining phase-B share
@@ -548,7 +682,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
           } else {
             bulk_g2s_stream(dst, src, bytes, cb.full + st, pol);
           }
-          if (ph == 0 && prefetch_b) prefetch_b_bytes(pf_step);
+          if (ph == 0 && prefetch_b && it >= NST) prefetch_b_bytes(pf_step);
         }
       }
       TRACE_AT(3);
@@ -556,7 +690,8 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
     }
   } else if (warp == SK_W_ACT) {
     // ------------------------------------------------------------------ activation staging + f16 conversion
-    int k = 0;  // non-empty segments so far
+    int k = 0;                 // non-empty segments so far
+    uint32_t land0 = 0, land1 = 0;  // landings per buffer (phase parity of act_land)
     for (int s = 0; s < nseg; ++s) {
       int ph, job;
       long long u0, u1;
@@ -567,6 +702,15 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
       const int K = ph ? p.I : p.H;
       const int ntok = min(jb.z, L.rows);
       uint8_t* dst = bufs + (size_t)b * L.rows * L.pitch;
+      if (xpre && ph == 0) {  // phase-A segments precede every phase-B one, so both buffers still hold the row
+        if (lane == 0) {
+          if (k >= NBUF) mbar_wait(cb.act_empty + b, ((k / NBUF) + 1) & 1, p.timeout_ns, status);
+          mbar_arrive(cb.act_full + b);
+        }
+        __syncwarp();
+        ++k;
+        continue;
+      }
       if (lane == 0) {
         if (k >= NBUF) mbar_wait(cb.act_empty + b, ((k / NBUF) + 1) & 1, p.timeout_ns, status);
         if (ph == 1) {
@@ -582,7 +726,8 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
         }
       }
       __syncwarp();
-      mbar_wait(cb.act_land + b, (k / NBUF) & 1, p.timeout_ns, status);
+      const uint32_t lpar = (b ? land1++ : land0++) & 1;
+      mbar_wait(cb.act_land + b, lpar, p.timeout_ns, status);
       if (lane == 0) TRACE_ONCE(17);
       sk_rows_to_f16(dst, L.pitch, ntok, K, cb.xexp[b]);
       __syncwarp();
@@ -593,46 +738,6 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
       ++k;
     }
     if (lane == 0) TRACE_AT(20);
-  } else if (warp == SK_W_SIG) {
-    // ------------------------------------------------------------------ signalling
-    int k = 0;
-    for (int s = 0; s < nseg; ++s) {
-      int ph, job;
-      long long u0, u1;
-      segs.at(s, ph, job, u0, u1);
-      if (u1 <= u0) continue;
-      const int slot = k % SK_SEG_RING;
-      const int want = (int)(u1 - u0);
-      // all units of the segment reduced and written by the epilogue warps (CTA-scope release, acquire here)
-      if (lane == 0) {
-        const uint64_t t0 = gtimer();
-        while (*reinterpret_cast<volatile int*>(&cb.seg_cnt[slot]) < want) {
-          __nanosleep(200);
-          if (gtimer() - t0 > p.timeout_ns) {
-            set_status(status, XCB_STATUS_DEVICE_TIMEOUT);
-            break;
-          }
-        }
-      }
-      __syncwarp();
-      __threadfence();  // cumulative: publishes the epilogue writes GPU-wide before the counters move
-      if (lane == 0) {
-        cb.seg_cnt[slot] = 0;
-        *reinterpret_cast<volatile int*>(&cb.seg_gen[slot]) = k / SK_SEG_RING + 1;
-      }
-      if (ph == 0) {
-        if (lane == 0) atomicAdd(p.doneA + job, want);
-      } else if (!p.grid_combine) {
-        // one count per 16-row block; the CTA that completes a block combines it (all its threads, at the end)
-        for (long long u = u0 + lane; u < u1; u += 32) {
-          const int rb = (int)(u - (long long)job * nrbB);
-          if (atomicAdd(p.rbcnt + rb, 1) == njobs - 1) cb.list[atomicAdd(&cb.nlist, 1)] = rb;
-        }
-        __syncwarp();
-      }
-      ++k;
-    }
-    if (lane == 0) TRACE_AT(21);
   } else if (warp >= SK_W_EPI) {
     // ------------------------------------------------------------------ reduction + epilogue
     // slot lane l holds the partial of accumulator lane (g, t) = (l % 8, l / 8): rows g, g + 8; tokens 2t, 2t + 1
@@ -712,23 +817,29 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
               }
             }
           }
-          // hand the finished unit to the signalling warp (CTA-scope release of the epilogue writes)
+          // count the finished unit; the warp that completes the segment publishes it GPU-wide (the CTA-scope
+          // fence orders this warp's writes before its count; the other warp's GPU-scope fence, issued after it
+          // observed every count of the segment, is cumulative)
           __syncwarp();
+          int done = 0;
           if (lane == 0) {
-            const int sl = k % SK_SEG_RING;
-            const int want = k / SK_SEG_RING;
-            if (*reinterpret_cast<volatile int*>(&cb.seg_gen[sl]) < want) {
-              const uint64_t t0 = gtimer();
-              while (*reinterpret_cast<volatile int*>(&cb.seg_gen[sl]) < want) {
-                __nanosleep(100);
-                if (gtimer() - t0 > p.timeout_ns) {
-                  set_status(status, XCB_STATUS_DEVICE_TIMEOUT);
-                  break;
-                }
+            __threadfence_block();
+            done = atomicAdd(&cb.seg_cnt[k % SK_SEG_RING], 1) + 1;
+          }
+          done = __shfl_sync(0xffffffffu, done, 0);
+          if (done == nunits) {
+            __threadfence();
+            if (lane == 0) cb.seg_cnt[k % SK_SEG_RING] = 0;
+            if (ph == 0) {
+              if (lane == 0) atomicAdd(p.doneA + job, nunits);
+            } else if (!p.grid_combine) {
+              // one count per 16-row block; the CTA that completes a block combines it (all threads, at the end)
+              for (long long u = u0 + lane; u < u1; u += 32) {
+                const int rb2 = (int)(u - (long long)job * nrbB);
+                if (atomicAdd(p.rbcnt + rb2, 1) == njobs - 1) cb.list[atomicAdd(&cb.nlist, 1)] = rb2;
               }
             }
-            __threadfence_block();
-            atomicAdd(&cb.seg_cnt[sl], 1);
+            __syncwarp();
           }
         }
       }
@@ -746,9 +857,8 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
     bool pend = false;
     int fpend = 0;
     float psc0 = 1.f, psc1 = 1.f;
-    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};  // set 0 (two chains)
-    float b0[4] = {0.f, 0.f, 0.f, 0.f}, b1[4] = {0.f, 0.f, 0.f, 0.f};  // set 1
-    auto deposit = [&](float* c0, float* c1) {  // write a finished set into its slot and clear it
+    float sa[2][4] = {}, sb[2][4] = {};  // the two accumulator sets, two chains each
+    auto deposit = [&](float (&c)[2][4]) {  // write a finished set into its slot and clear it
       const int slot = fpend % SK_NSLOT;
       TRACE_T0(t_sf);
       if (fpend >= SK_NSLOT) mbar_wait(cb.slot_free + slot, ((fpend / SK_NSLOT) + 1) & 1, p.timeout_ns, status);
@@ -756,11 +866,17 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
         TRACE_SPAN(14, t_sf);
         TRACE_ADD(18, 1);
       }
-      if (wr)
-        *reinterpret_cast<float4*>(red + slot * (L.red_slot / 4) + (warp * L.rl + t * 8 + g) * 4) =
-            make_float4((c0[0] + c1[0]) * psc0, (c0[1] + c1[1]) * psc1, (c0[2] + c1[2]) * psc0, (c0[3] + c1[3]) * psc1);
+      if (wr) {
+        float v[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) c0[i] = c1[i] = 0.f;
+        for (int i = 0; i < 4; ++i) v[i] = c[0][i] + c[1][i];
+        *reinterpret_cast<float4*>(red + slot * (L.red_slot / 4) + (warp * L.rl + t * 8 + g) * 4) =
+            make_float4(v[0] * psc0, v[1] * psc1, v[2] * psc0, v[3] * psc1);
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) c[j][i] = 0.f;
       __syncwarp();
       if (lane == 0) mbar_arrive(cb.slot_full + slot);
       pend = false;
@@ -801,9 +917,9 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
           const uint8_t* xs = xrow + (size_t)(my0 % U) * 128;
           TRACE_T0(t_c);
           if (cur)
-            sk_run_per(PER, sl, xs, lane, t, b0, b1);
+            sk_run_per(PER, sl, xs, lane, t, sb);
           else
-            sk_run_per(PER, sl, xs, lane, t, a0, a1);
+            sk_run_per(PER, sl, xs, lane, t, sa);
           if (warp == 0) {
             __syncwarp();
             if (lane == 0) TRACE_SPAN(ph ? 31 : 23, t_c);
@@ -818,7 +934,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
         }
         if (pend) {
           TRACE_T0(t_d);
-          if (cur) deposit(a0, a1); else deposit(b0, b1);
+          if (cur) deposit(sa); else deposit(sb);
           if (warp == 0 && lane == 0) TRACE_SPAN(25, t_d);
         }
         if ((i + 1) % spe == 0) {
@@ -835,7 +951,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(SkinnyParams p) {
       // the segment's last set is written now, not after the next segment's first stage: the next segment's
       // activations may wait (phase B) on phase-A counters that this very set completes
       if (pend) {
-        if (cur) deposit(a0, a1); else deposit(b0, b1);
+        if (cur) deposit(sa); else deposit(sb);
       }
       ++k;
     }
@@ -938,7 +1054,7 @@ extern "C" int xcb_trace_clear() {
 }
 #endif
 
-int skinny_config(int* grid_out, int* smem_out, int H, int I, int job_tokens, int route_R) {
+int skinny_config(int* grid_out, SkLayout* plan, int H, int I, int job_tokens, int route_R) {
   static int cached_dev = -1, cached_sms = 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return XCB_ERR_CUDA;
@@ -951,7 +1067,7 @@ int skinny_config(int* grid_out, int* smem_out, int H, int I, int job_tokens, in
     cached_dev = dev;
   }
   *grid_out = cached_sms;  // one CTA per SM (the kernel takes nearly all shared memory)
-  *smem_out = L.total;
+  *plan = L;
   return XCB_OK;
 }
 
@@ -971,10 +1087,11 @@ bool skinny_supported(int H, int I) {
 }
 
 int launch_skinny(const SkinnyParams& p, cudaStream_t stream) {
-  int grid = 0, smem = 0;
-  int rc = skinny_config(&grid, &smem, p.H, p.I, p.job_tokens, p.small_route ? p.T * p.k : 0);
+  int grid = 0;
+  SkLayout plan;
+  int rc = skinny_config(&grid, &plan, p.H, p.I, p.job_tokens, p.small_route ? p.T * p.k : 0);
   if (rc != XCB_OK) return rc;
-  skinny_kernel<<<grid, SK_THREADS, smem, stream>>>(p);
+  skinny_kernel<<<grid, SK_THREADS, plan.total, stream>>>(p, plan);
   return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
 }
 
