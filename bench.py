@@ -2,7 +2,9 @@
 
 Default workload (N=1): the DeepSeek-V3-shaped decode layer (configuration 2: T=1, H=7168, I=2048, E=256,
 top-8), HBM-bound.  ``--config prefill`` runs configuration 3 (T=4096, biased router), ``--config qwen:T`` the
-Qwen3-30B-A3B shape.  A step is one full layer (router + experts + combine) over one batch.
+Qwen3-30B-A3B shape, ``--config ep`` configuration 5 (16384 tokens per GPU, Zipf-biased router).  A step is one
+full layer (router + experts + combine) over one batch.  With N > 1 GPUs (torchrun) the layer runs expert-parallel:
+each GPU holds E / N experts and its own tokens, which travel to the experts' GPUs and back (weak scaling).
 
 * ``value``: tokens/s over all ranks, inputs resident in HBM, CUDA events on the launching stream, max over ranks.
   Weights are 6.3 GB resident (>> 126 MB L2) and every step uses a different input from a pool of 64, so each
@@ -32,6 +34,9 @@ if ROOT not in sys.path:
 CONFIGS = {
     "decode": dict(workload="deepseek_v3_moe_decode", E=256, H=7168, I=2048, T=1, k=8, bias_std=0.0),
     "prefill": dict(workload="deepseek_v3_moe_prefill", E=256, H=7168, I=2048, T=4096, k=8, bias_std=0.5),
+    # configuration 5: 16384 tokens per GPU, Zipf(s=1.1) router bias toward low expert ids (the worst case for
+    # contiguous expert shards: bias_e = -1.1 ln(e + 1))
+    "ep": dict(workload="deepseek_v3_moe_ep", E=256, H=7168, I=2048, T=16384, k=8, bias_std=0.0, zipf=1.1),
 }
 METRIC = "MoE layer tokens/s; decode HBM GB/s & prefill TFLOPS vs B200 roofline"
 
@@ -42,6 +47,7 @@ def config_for(name: str, experts: int = 0) -> dict:
         cfg = dict(workload=f"qwen3_30b_a3b_moe_T{T}", E=128, H=2048, I=768, T=T, k=8, bias_std=0.0)
     else:
         cfg = dict(CONFIGS[name])
+    cfg.setdefault("zipf", 0.0)
     if experts:
         cfg["E"] = experts
         cfg["workload"] += f"_E{experts}"
@@ -166,14 +172,15 @@ def run_xcb(a, cfg, rank, world, dist):
     layer = PreparedMoE(*weights.values())
     cpu = None
     if rank == 0 and not a.no_cpu_baseline:
-        x0, l0 = synth.make_inputs(T, H, E, seed=1, device=dev, bias_std=cfg["bias_std"])
+        x0, l0 = synth.make_inputs(T, H, E, seed=1, device=dev, bias_std=cfg["bias_std"], zipf_s=cfg["zipf"])
         cpu = cpu_oracle_sample(weights, x0, l0, k, min(T, a.cpu_sample_tokens))
     del weights                                       # only the packed copy stays resident
     torch.cuda.empty_cache()
     P = max(1, a.pool if T <= 64 else 2)
     xs, lgs = [], []
     for i in range(P):
-        x, lg = synth.make_inputs(T, H, E, seed=1000 * rank + i + 1, device=dev, bias_std=cfg["bias_std"])
+        x, lg = synth.make_inputs(T, H, E, seed=1000 * rank + i + 1, device=dev, bias_std=cfg["bias_std"],
+                                  zipf_s=cfg["zipf"])
         xs.append(x)
         lgs.append(lg)
     outs = [torch.empty((T, H), dtype=torch.bfloat16, device=dev) for _ in range(P)]
@@ -233,6 +240,105 @@ def run_xcb(a, cfg, rank, world, dist):
         ms, kern_ms, e2e_ms = t.tolist()
         e2e_ms = e2e_ms or None
     return finish(a, cfg, world, ms, kern_ms, e2e_ms, u_avg, P, clk, cpu)
+
+
+def run_xcb_ep(a, cfg, rank, world, dist):
+    """N > 1: expert parallelism.  Every rank holds E / N experts and its own T tokens (weak scaling); a step is one
+    layer over every rank's tokens: router, dispatch (NCCL all-to-all over NVLink), the local experts, return and
+    combine.  Timed with CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as td
+
+    from xcalibur_b200 import synth
+    from xcalibur_b200.ep import ExpertParallelMoE
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    E, H, I, T, k = cfg["E"], cfg["H"], cfg["I"], cfg["T"], cfg["k"]
+    epr = E // world
+    weights = synth.make_weights(E, H, I, seed=1234, device=dev)      # same layer on every rank; keep this shard
+    shard = {n: t[rank * epr:(rank + 1) * epr].contiguous() for n, t in weights.items()}
+    del weights
+    torch.cuda.empty_cache()
+    layer = ExpertParallelMoE(*shard.values(), total_experts=E)
+    del shard
+    P = max(1, a.pool if T <= 64 else 2)
+    xs, lgs = [], []
+    for i in range(P):
+        x, lg = synth.make_inputs(T, H, E, seed=1000 * rank + i + 1, device=dev, bias_std=cfg["bias_std"],
+                                  zipf_s=cfg["zipf"])
+        xs.append(x)
+        lgs.append(lg)
+    for i in range(max(3, a.warmup)):
+        layer.forward(xs[i % P], lgs[i % P], k)
+    torch.cuda.synchronize()
+    if layer.ops.device_status() or layer.ops.layer.check_device_status():
+        raise RuntimeError("device status bits set during warm-up")
+    U, R = [], []
+    for i in range(P):  # experts this rank streams and routes it computes, per input
+        layer.forward(xs[i], lgs[i], k)
+        rid = layer.last["recv_ids"]
+        loc = rid[(rid >= rank * epr) & (rid < (rank + 1) * epr)]
+        U.append(int(torch.unique(loc).numel()))
+        R.append(int(loc.numel()))
+    K = a.steps
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev.index)
+    td.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    start.record()
+    for i in range(K):
+        layer.forward(xs[i % P], lgs[i % P], k)
+    end.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    td.barrier()
+    ms = start.elapsed_time(end) / K
+    # end to end: pinned host inputs in, output out, every step
+    e2e_ms = None
+    if not a.no_e2e:
+        xh = [x.cpu().pin_memory() for x in xs]
+        lh = [l.cpu().pin_memory() for l in lgs]
+        oh = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+        xd, ld = torch.empty_like(xs[0]), torch.empty_like(lgs[0])
+        td.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(K):
+            xd.copy_(xh[i % P], non_blocking=True)
+            ld.copy_(lh[i % P], non_blocking=True)
+            oh.copy_(layer.forward(xd, ld, k), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / K
+    if layer.ops.device_status() or layer.ops.layer.check_device_status():
+        raise RuntimeError("device status bits set in the timed region")
+    t = torch.tensor([ms, e2e_ms or 0.0], dtype=torch.float64, device=dev)
+    td.all_reduce(t, op=td.ReduceOp.MAX)
+    ms, e2e_ms = t[0].item(), (t[1].item() or None)
+    u_avg = sum(U[i % P] for i in range(K)) / K
+    r_avg = sum(R[i % P] for i in range(K)) / K
+    res = finish(a, cfg, world, ms, ms, e2e_ms, u_avg, P, clk, None)
+    hbm, bf16, bf16_sus, src = load_peaks()
+    if T <= 64:
+        achieved = (synth.layer_bytes(1, H, I) * u_avg + 2 * T * H * 2) / (ms * 1e-3) / 1e9
+        res["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                           "frac": round(achieved / hbm, 4), "peak_source": src, "traffic": None}
+    else:
+        achieved = 2 * r_avg * 3 * H * I / (ms * 1e-3) / 1e12
+        res["roofline"] = {"bound": "tensor", "achieved": round(achieved, 1), "peak": bf16_sus, "unit": "TFLOP/s",
+                           "frac": round(achieved / bf16_sus, 4), "peak_source": src + " (sustained)", "traffic": None}
+    res["roofline"]["kernel"] = "whole expert-parallel step per rank (router, dispatch, local experts, combine)"
+    res["roofline"]["step_ms"] = round(ms, 5)
+    res["config"]["parallelism"] = f"ep{world}"
+    res["config"]["experts_per_gpu"] = epr
+    res["config"]["l2"] = (f"{P} rotating inputs per rank; {u_avg:.1f} distinct local experts and {r_avg:.0f} local "
+                           f"routes per rank per step")
+    # per step: top-k, plan, gather, combine + the local layer (one decode launch, or router + gather + two grouped
+    # GEMMs + combine on the prefill path)
+    res["gpu_launches"] = K * (4 + (1 if T * k <= 256 else 5))
+    return res
 
 
 def run_e2e(a, layer, xs, lgs, k, P, dist):
@@ -319,7 +425,7 @@ def finish(a, cfg, world, ms, kern_ms, e2e_ms, u_avg, P, clk, cpu):
         "gpu_launches": a.steps * (1 if T * k <= 256 and T <= 32 else 5),
         "clocks": clk,
     }
-    if cpu is not None:
+    if cpu is not None and world == 1:
         secs, n, cores = cpu
         res["cpu_baseline"] = {"value": round(n / secs, 4), "unit": "tokens/s", "cores": cores, "kind": "port",
                                "sample": f"{n} token(s) of {cfg['workload']} through the CPU oracle "
@@ -379,7 +485,7 @@ def main():
         td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         dist = td
     try:
-        res = run_xcb(a, cfg, rank, world, dist)
+        res = run_xcb_ep(a, cfg, rank, world, dist) if world > 1 else run_xcb(a, cfg, rank, world, dist)
         if rank == 0:
             print(json.dumps(res), flush=True)
     finally:

@@ -158,6 +158,35 @@ int xcb_moe_read_status(void* workspace, int32_t* device_status, cudaStream_t st
 int xcb_hbm_probe(const void* src, size_t bytes, int mode, int chunk, int stages, int ctas_per_sm, int threads,
                   const long long* regions, int nreg, int32_t* status, float* sink, cudaStream_t stream);
 
+/* ---- expert parallelism ----
+ * The reference models an expert-parallel rank only as a local expert range whose non-local routes are masked
+ * (moe_w4a16.py:105-110, :513-520); the exchange between ranks was its harness's job.  These helpers give the
+ * expert-parallel layer its dispatch and combine: experts are held contiguously, experts_per_rank per rank, and a
+ * token is sent once to every rank holding one of its experts, with its full top-k row (the receiving rank's
+ * xcb_moe_forward masks the experts it does not hold). */
+
+/* Router alone: softmax -> top-k -> renormalise per token (ties to the lower expert id), ids int32 [T, k] and
+ * weights fp32 [T, k] for all E experts.  Same selection and weights as xcb_moe_forward's router. */
+int xcb_moe_topk(const float* logits, int32_t T, int32_t E, int32_t k, int32_t* ids, float* wts, cudaStream_t stream);
+
+/* Dispatch plan of one rank's T tokens over G ranks (G <= 32): counts int32 [G] (tokens for each rank),
+ * send_tok int32 [G, T] (row d: the tokens for rank d in token order, first counts[d] valid), send_pos int32 [T, G]
+ * (position of token t in rank d's list, or -1).  status gets XCB_STATUS_BAD_EXPERT for an id outside
+ * [0, G * experts_per_rank). */
+int xcb_ep_plan(const int32_t* ids, int32_t T, int32_t k, int32_t experts_per_rank, int32_t G, int32_t* counts,
+                int32_t* send_tok, int32_t* send_pos, int32_t* status, cudaStream_t stream);
+
+/* Send buffer in destination order (rank 0's rows first): x_out bf16 [sum(counts), H], ids_out int32 [.., k],
+ * w_out fp32 [.., k]. */
+int xcb_ep_gather(const uint16_t* x, const int32_t* ids, const float* wts, int32_t T, int32_t H, int32_t k, int32_t G,
+                  const int32_t* counts, const int32_t* send_tok, uint16_t* x_out, int32_t* ids_out, float* w_out,
+                  cudaStream_t stream);
+
+/* out[t] = bf16(sum over ranks d in rank order of parts[row of (t, d)]), parts bf16 [sum(counts), H] in the send
+ * buffer's order (each rank returns the partial sums of the rows it received, in the order received). */
+int xcb_ep_combine(const uint16_t* parts, const int32_t* counts, const int32_t* send_pos, int32_t T, int32_t H,
+                   int32_t G, uint16_t* out, cudaStream_t stream);
+
 /* Quantise fp32 weights [E, R, K] to NVFP4 (gs = amax/(6*448) per expert, sf = e4m3(block_amax/6/gs),
  * codes RNE to E2M1): codes [E, R, K/2], sf [E, R, K/16], gs [E].  A utility for synthetic weights; the
  * reference receives already-quantised weights.  amax_scratch: device float [E] (zeroed by this call). */

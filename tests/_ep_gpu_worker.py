@@ -1,0 +1,37 @@
+"""Worker of the two-GPU expert-parallel test (test infrastructure): one rank per GPU over NCCL."""
+from __future__ import annotations
+
+import datetime
+import os
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+
+def nccl_worker(rank, world, port, E, H, I, T, k, seed, result_dir):
+    from xcalibur_b200 import PreparedMoE, synth
+    from xcalibur_b200.ep import ExpertParallelMoE
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        w = synth.make_weights(E, H, I, seed=seed, device=dev)           # the whole layer, same on every rank
+        epr = E // world
+        shard = {n: t[rank * epr:(rank + 1) * epr].contiguous() for n, t in w.items()}
+        ep = ExpertParallelMoE(*shard.values(), total_experts=E)
+        full = PreparedMoE(*w.values())
+        x, logits = synth.make_inputs(T, H, E, seed=seed + 1 + rank, device=dev, bias_std=0.5)
+        out_ep = ep.forward(x, logits, k)
+        out_1 = full.forward(x, logits, k)
+        torch.cuda.synchronize()
+        st = ep.ops.device_status() | ep.ops.layer.check_device_status() | full.check_device_status()
+        np.save(os.path.join(result_dir, f"nccl_{rank}.npy"),
+                np.stack([out_ep.view(torch.int16).cpu().numpy().view(np.uint16),
+                          out_1.view(torch.int16).cpu().numpy().view(np.uint16)]))
+        np.save(os.path.join(result_dir, f"nccl_status_{rank}.npy"), np.array([st]))
+    finally:
+        dist.destroy_process_group()

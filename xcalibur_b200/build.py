@@ -16,7 +16,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libxcb_moe.so")
-SOURCES = ["api.cu", "route.cu", "skinny.cu", "wide.cu", "pack.cu", "probe.cu"]
+SOURCES = ["api.cu", "route.cu", "skinny.cu", "wide.cu", "pack.cu", "probe.cu", "ep.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

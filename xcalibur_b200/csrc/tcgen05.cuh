@@ -69,7 +69,7 @@ __device__ __forceinline__ void tc_ld_x32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// 2-D tiled TMA load (no multicast) completing on an mbarrier.  x (the inner coordinate) must be a multiple of
+// 2-D tiled TMA load into this CTA's shared memory, completing on an mbarrier.  x (the inner coordinate) must be a multiple of
 // 8 bf16 elements so the copy starts on a 16-byte boundary.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
   asm volatile(

@@ -1,0 +1,147 @@
+"""Expert-parallel NVFP4 MoE layer: the experts are sharded contiguously over the ranks of a torch.distributed
+group, every rank routes its own tokens, and tokens travel to the ranks that hold their experts and back.
+
+The reference models an expert-parallel rank only as a local expert range whose non-local routes it masks
+(kernels/moe_w4a16_h200/moe_w4a16.py:105-110, :513-520); the cross-rank sum was its harness's job.  Here one call
+is, on every rank (``forward``):
+
+1. ``xcb_moe_topk``: top-k over all experts for this rank's tokens;
+2. ``xcb_ep_plan``: a token goes once to every rank holding one of its experts (in token order); the per-rank
+   counts are exchanged (all-to-all of G integers, read on the host for the split sizes);
+3. ``xcb_ep_gather`` + all-to-all: the token rows with their full top-k ids and weights;
+4. the local layer (``PreparedMoE`` with ``expert_offset``) on the received rows: routes to experts this rank does
+   not hold contribute nothing, so each received row yields this rank's partial sum;
+5. all-to-all back in the same order, then ``xcb_ep_combine``: out[t] = bf16(sum of its partials in rank order).
+
+The transport is ``torch.distributed.all_to_all_single`` (NCCL over NVLink on GPUs).  The per-rank steps run in the
+C-ABI library; ``_ops`` exists so that tests can substitute a CPU model of those steps and check the exchange
+protocol itself with the gloo backend (world size 2) on machines without GPUs.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ._lib import check
+from .moe import PreparedMoE
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class CudaEpOps:
+    """The per-rank steps of an expert-parallel call, on the GPU through the C-ABI."""
+
+    def __init__(self, layer: PreparedMoE):
+        self.layer = layer
+        self.lib = layer.lib
+        self.device = layer.device
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def topk(self, logits: torch.Tensor, k: int):
+        T, E = logits.shape
+        ids = torch.empty((T, k), dtype=torch.int32, device=self.device)
+        wts = torch.empty((T, k), dtype=torch.float32, device=self.device)
+        logits = logits.to(torch.float32).contiguous()
+        check(self.lib.xcb_moe_topk(logits.data_ptr(), T, E, k, ids.data_ptr(), wts.data_ptr(), _stream(self.device)),
+              "xcb_moe_topk")
+        return ids, wts
+
+    def plan(self, ids: torch.Tensor, experts_per_rank: int, world: int):
+        T, k = ids.shape
+        counts = torch.empty(world, dtype=torch.int32, device=self.device)
+        send_tok = torch.empty((world, max(T, 1)), dtype=torch.int32, device=self.device)
+        send_pos = torch.empty((max(T, 1), world), dtype=torch.int32, device=self.device)
+        check(self.lib.xcb_ep_plan(ids.data_ptr(), T, k, experts_per_rank, world, counts.data_ptr(),
+                                   send_tok.data_ptr(), send_pos.data_ptr(), self.status.data_ptr(),
+                                   _stream(self.device)), "xcb_ep_plan")
+        return counts, send_tok, send_pos
+
+    def gather(self, x, ids, wts, counts, send_tok, total: int):
+        T, H = x.shape
+        k = ids.shape[1]
+        xs = torch.empty((total, H), dtype=torch.bfloat16, device=self.device)
+        ids_s = torch.empty((total, k), dtype=torch.int32, device=self.device)
+        w_s = torch.empty((total, k), dtype=torch.float32, device=self.device)
+        if total:
+            check(self.lib.xcb_ep_gather(x.data_ptr(), ids.data_ptr(), wts.data_ptr(), T, H, k, counts.numel(),
+                                         counts.data_ptr(), send_tok.data_ptr(), xs.data_ptr(), ids_s.data_ptr(),
+                                         w_s.data_ptr(), _stream(self.device)), "xcb_ep_gather")
+        return xs, ids_s, w_s
+
+    def local(self, xr, ids_r, w_r, post_norm: bool):
+        if xr.shape[0] == 0:
+            return torch.empty((0, xr.shape[1]), dtype=torch.bfloat16, device=self.device)
+        return self.layer.forward(xr, None, topk_ids=ids_r, topk_weights=w_r, post_norm=post_norm)
+
+    def combine(self, parts, counts, send_pos, T: int):
+        H = parts.shape[1]
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=self.device)
+        if T:
+            check(self.lib.xcb_ep_combine(parts.data_ptr() if parts.numel() else None, counts.data_ptr(),
+                                          send_pos.data_ptr(), T, H, counts.numel(), out.data_ptr(),
+                                          _stream(self.device)), "xcb_ep_combine")
+        return out
+
+    def device_status(self) -> int:
+        """Status bits of the plan kernel (XCB_STATUS_BAD_EXPERT), read and cleared."""
+        v = int(self.status.item())
+        self.status.zero_()
+        return v
+
+
+class ExpertParallelMoE:
+    """This rank's share of an expert-parallel MoE layer.
+
+    ``w13 .. w2_gs`` hold experts ``[rank * E / G, (rank + 1) * E / G)`` of ``total_experts = E`` (reference layout,
+    ``moe_w4a16.py:72-79``); every rank of ``group`` calls ``forward`` with its own tokens, collectively."""
+
+    def __init__(self, w13, w13_sf, w13_gs, w2, w2_sf, w2_gs, *, total_experts: int, group=None,
+                 post_norm_w=None, _ops=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if total_experts % self.world:
+            raise ValueError(f"{total_experts} experts do not split evenly over {self.world} ranks")
+        self.E = int(total_experts)
+        self.epr = self.E // self.world
+        if w13.shape[0] != self.epr:
+            raise ValueError(f"rank {self.rank} must hold {self.epr} experts, got {w13.shape[0]}")
+        self.post_norm = post_norm_w is not None
+        if _ops is None:
+            layer = PreparedMoE(w13, w13_sf, w13_gs, w2, w2_sf, w2_gs, post_norm_w, total_experts=self.E,
+                                expert_offset=self.rank * self.epr)
+            _ops = CudaEpOps(layer)
+        self.ops = _ops
+        self.last = {}
+
+    def _a2a(self, send: torch.Tensor, send_splits, recv_splits, trailing) -> torch.Tensor:
+        out = torch.empty((sum(recv_splits), *trailing), dtype=send.dtype, device=send.device)
+        dist.all_to_all_single(out, send, output_split_sizes=list(recv_splits), input_split_sizes=list(send_splits),
+                               group=self.group)
+        return out
+
+    def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor, top_k: int) -> torch.Tensor:
+        """One layer over this rank's tokens (collective over the group): bf16 [T, H] out."""
+        x = hidden_states.contiguous()
+        T, H = x.shape
+        if tuple(router_logits.shape) != (T, self.E):
+            raise ValueError(f"router_logits must be [T, {self.E}]")
+        ids, wts = self.ops.topk(router_logits, top_k)
+        counts, send_tok, send_pos = self.ops.plan(ids, self.epr, self.world)
+        recv_counts = torch.empty_like(counts)
+        dist.all_to_all_single(recv_counts, counts, group=self.group)
+        send_splits = [int(v) for v in counts.cpu().tolist()]
+        recv_splits = [int(v) for v in recv_counts.cpu().tolist()]
+        xs, ids_s, w_s = self.ops.gather(x, ids, wts, counts, send_tok, sum(send_splits))
+        xr = self._a2a(xs, send_splits, recv_splits, (H,))
+        ids_r = self._a2a(ids_s, send_splits, recv_splits, (top_k,))
+        w_r = self._a2a(w_s, send_splits, recv_splits, (top_k,))
+        parts = self.ops.local(xr, ids_r, w_r, self.post_norm)
+        back = self._a2a(parts, recv_splits, send_splits, (H,))
+        out = self.ops.combine(back, counts, send_pos, T)
+        self.last = {"ids": ids, "wts": wts, "send": send_splits, "recv": recv_splits, "recv_ids": ids_r}
+        return out
+
+    __call__ = forward
