@@ -18,7 +18,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("T", [1, 7])
+@pytest.mark.parametrize("T", [1, 7, 40])  # 40 > DENSE_MAX_TOKENS: the planned, uneven exchange
 def test_ep_two_ranks_match_single_process(tmp_path, T):
     world, E, H, I, k = 2, 8, 256, 256, 4
     mp.spawn(gloo_worker, args=(world, _free_port(), E, H, I, T, k, 123, str(tmp_path)), nprocs=world, join=True)

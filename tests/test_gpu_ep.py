@@ -19,7 +19,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("T", [1, 600])
+@pytest.mark.parametrize("T", [1, 600])  # dense exchange, planned exchange
 def test_ep_two_gpus_match_single_gpu(tmp_path, T):
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")

@@ -13,6 +13,9 @@ is, on every rank (``forward``):
    not hold contribute nothing, so each received row yields this rank's partial sum;
 5. all-to-all back in the same order, then ``xcb_ep_combine``: out[t] = bf16(sum of its partials in rank order).
 
+Small batches (at most DENSE_MAX_TOKENS tokens per rank, decode) skip the plan: every token goes to every rank with
+equal splits, so the step has three collectives and no host synchronisation.
+
 The transport is ``torch.distributed.all_to_all_single`` (NCCL over NVLink on GPUs).  The per-rank steps run in the
 C-ABI library; ``_ops`` exists so that tests can substitute a CPU model of those steps and check the exchange
 protocol itself with the gloo backend (world size 2) on machines without GPUs.
@@ -122,13 +125,46 @@ class ExpertParallelMoE:
                                group=self.group)
         return out
 
+    # Up to this many tokens per rank a call is exchanged densely: every token goes to every rank (fixed, equal
+    # splits), so no counts exchange and no host synchronisation are needed; a rank holding none of a token's experts
+    # returns a zero partial for it.  Small batches (decode) are latency-bound, and this halves their collectives.
+    DENSE_MAX_TOKENS = 32
+
+    def _dense(self, x, ids, wts, top_k):
+        T, H = x.shape
+        G = self.world
+        key = (T, G, x.device)
+        if self.last.get("dense_key") != key:  # combine tables of the fixed layout: token t's row from rank d is d*T+t
+            dev = x.device
+            self._dense_counts = torch.full((G,), T, dtype=torch.int32, device=dev)
+            self._dense_pos = torch.arange(T, dtype=torch.int32, device=dev)[:, None].expand(T, G).contiguous()
+            self.last["dense_key"] = key
+        xs = x.unsqueeze(0).expand(G, T, H).reshape(G * T, H).contiguous()
+        meta = torch.cat([ids, wts.view(torch.int32)], dim=1).unsqueeze(0).expand(G, T, 2 * top_k)
+        meta = meta.reshape(G * T, 2 * top_k).contiguous()
+        xr = torch.empty_like(xs)
+        mr = torch.empty_like(meta)
+        dist.all_to_all_single(xr, xs, group=self.group)
+        dist.all_to_all_single(mr, meta, group=self.group)
+        ids_r = mr[:, :top_k].contiguous()
+        w_r = mr[:, top_k:].contiguous().view(torch.float32)
+        parts = self.ops.local(xr, ids_r, w_r, self.post_norm)
+        back = torch.empty_like(parts)
+        dist.all_to_all_single(back, parts, group=self.group)
+        out = self.ops.combine(back, self._dense_counts, self._dense_pos, T)
+        self.last.update({"ids": ids, "wts": wts, "send": [T] * G, "recv": [T] * G, "recv_ids": ids_r})
+        return out
+
     def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor, top_k: int) -> torch.Tensor:
-        """One layer over this rank's tokens (collective over the group): bf16 [T, H] out."""
+        """One layer over this rank's tokens (collective over the group): bf16 [T, H] out.  Every rank must pass
+        the same token count when it is at most DENSE_MAX_TOKENS (the dense exchange uses equal splits)."""
         x = hidden_states.contiguous()
         T, H = x.shape
         if tuple(router_logits.shape) != (T, self.E):
             raise ValueError(f"router_logits must be [T, {self.E}]")
         ids, wts = self.ops.topk(router_logits, top_k)
+        if 0 < T <= self.DENSE_MAX_TOKENS:
+            return self._dense(x, ids, wts, top_k)
         counts, send_tok, send_pos = self.ops.plan(ids, self.epr, self.world)
         recv_counts = torch.empty_like(counts)
         dist.all_to_all_single(recv_counts, counts, group=self.group)
@@ -141,7 +177,7 @@ class ExpertParallelMoE:
         parts = self.ops.local(xr, ids_r, w_r, self.post_norm)
         back = self._a2a(parts, recv_splits, send_splits, (H,))
         out = self.ops.combine(back, counts, send_pos, T)
-        self.last = {"ids": ids, "wts": wts, "send": send_splits, "recv": recv_splits, "recv_ids": ids_r}
+        self.last.update({"ids": ids, "wts": wts, "send": send_splits, "recv": recv_splits, "recv_ids": ids_r})
         return out
 
     __call__ = forward
