@@ -12,7 +12,7 @@
 //   combine  out[t] = bf16(sum_s w_s (* rsqrt(ss/H + 1e-8)) y[pos[t, s]])          (slot order, as the reference)
 //
 // wide_kernel is persistent (one CTA per SM, 640 threads, static round-robin over tiles).  A tile is 128 packed
-// weight rows of one expert x up to 256 of its tokens, the full reduction length:
+// weight rows of one expert x up to 192 of its tokens, the full reduction length:
 //
 //   warp 0       streams the tile's packed weights (18 KB bulk copies, the prefill layout) into a 4-stage ring;
 //   warp 2       loads the tokens' activation rows into a 4-stage ring: one 2-D TMA box (64 k x 64, 128 or 256
@@ -27,9 +27,11 @@
 //   warps 12-19  drain the fp32 accumulator (tcgen05.ld; two warps per lane quarter, one per 128-token half)
 //                through the epilogue and release it.
 //
-// Tensor memory (512 columns): an A ring of 8 chunks x 32 columns, then one 256-column accumulator.  The MMA
-// issue rate sets the shape: a 128 x N x 16 bf16 MMA takes N/2 clocks for N >= 64 (44 clocks below), so wide
-// tiles amortise the per-instruction cost.  Every wait is bounded; a wait that runs out sets
+// Tensor memory (512 columns): an A ring of 4 chunks x 32 columns, then two 192-column accumulators, so the MMAs
+// of the next tile run while the epilogue drains the last one (with one accumulator the MMA warp waited for every
+// drain, ~16 % of the GEMM time at the DeepSeek-V3 prefill size).  The MMA issue rate sets the shape: a
+// 128 x N x 16 bf16 MMA takes N/2 clocks for N >= 64 (44 clocks below), so wide tiles amortise the per-instruction
+// cost.  Every wait is bounded; a wait that runs out sets
 // XCB_STATUS_DEVICE_TIMEOUT and an abort flag that ends every role, and the kernel drains its copies and MMAs
 // before it frees tensor memory.
 #include <cudaTypedefs.h>
@@ -42,13 +44,13 @@
 
 namespace xcb {
 
-constexpr int kWdTok = 256;       // tokens per tile (MMA N upper bound)
+constexpr int kWdTok = 192;       // tokens per tile (MMA N upper bound; two accumulators of this width)
 constexpr int kWdStage = 18432;   // packed bytes of 256 k x 128 rows
 constexpr int kWdChunk = 4608;    // packed bytes of 64 k x 128 rows
 constexpr int kWdWSt = 4;         // weight ring stages (power of two)
 constexpr int kWdBSt = 4;         // activation ring stages, 64 k x 256 rows bf16 each
 constexpr int kWdBBytes = 32768;
-constexpr int kWdASlots = 8;      // tensor-memory A ring, 32 columns each (power of two)
+constexpr int kWdASlots = 4;      // tensor-memory A ring, 32 columns each (power of two)
 #ifndef XCB_WD_NDQ
 #define XCB_WD_NDQ 2
 #endif
@@ -57,14 +59,17 @@ constexpr int kWdEpiWarp0 = 4 + 4 * kWdDq;
 constexpr int kWdEpiWarps = 8;     // two per tensor-memory lane quarter, one per 128-column half
 constexpr int kWdThreads = 32 * (kWdEpiWarp0 + kWdEpiWarps);
 constexpr int kWdXbuf = 4 * 2 * 32 * 17;  // SwiGLU exchange: [pair][gate|up][32 lanes][16 tokens + 1]
-constexpr int kWdNBar = 2 * kWdWSt + 2 * kWdASlots + 2 + 1;
+constexpr int kWdNBar = 2 * kWdWSt + 2 * kWdASlots + 4 + 1;
 constexpr size_t kWdOffB = (size_t)kWdWSt * kWdStage;  // 1024-aligned (swizzle atoms)
 constexpr size_t kWdOffX = kWdOffB + (size_t)kWdBSt * kWdBBytes;
 constexpr size_t kWdOffBar = kWdOffX + (size_t)kWdXbuf * 4;
 constexpr size_t kWdOffTab = kWdOffBar + (size_t)kWdNBar * 8;
 constexpr size_t kWdOffMisc = kWdOffTab + 2 * 516 * 4;
 constexpr size_t kWdSmem = kWdOffMisc + 64 + 1024;  // + slack to align the base to 1024
-constexpr uint32_t kWdDCol = 256;  // accumulator columns [256, 512); A ring [0, 256)
+// Tensor memory (512 columns): the A ring [0, 128), accumulator 0 [128, 320), accumulator 1 [320, 512): the MMAs
+// of tile i + 1 fill one accumulator while the epilogue drains tile i from the other.
+constexpr uint32_t kWdDCol = 32 * kWdASlots;
+static_assert(kWdDCol + 2 * kWdTok <= 512, "tensor memory columns");
 static_assert(kWdOffB % 1024 == 0, "activation ring must be 1024-aligned");
 static_assert(kWdSmem <= 227 * 1024, "prefill kernel shared memory");
 
@@ -166,9 +171,9 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
   // both the A slot (reused by chunk gc + 8) and the activation slot (reused by chunk gc + 4)
   uint64_t* ab_full = w_empty + kWdWSt;
   uint64_t* ab_empty = ab_full + kWdASlots;
-  uint64_t* d_full = ab_empty + kWdASlots;
-  uint64_t* d_empty = d_full + 1;
-  uint64_t* drain = d_empty + 1;
+  uint64_t* d_full = ab_empty + kWdASlots;  // [2]: accumulator b holds a finished tile
+  uint64_t* d_empty = d_full + 2;           // [2]: the epilogue drained accumulator b
+  uint64_t* drain = d_empty + 2;
   int* offs = reinterpret_cast<int*>(sm + kWdOffTab);
   int* tpre = offs + 516;
   volatile int* abrt = reinterpret_cast<volatile int*>(sm + kWdOffMisc);
@@ -186,8 +191,10 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
       mbar_init(ab_full + i, 5);  // 4 dequantising warps + the activation producer (with the box's bytes)
       mbar_init(ab_empty + i, 1);
     }
-    mbar_init(d_full, 1);
-    mbar_init(d_empty, kWdEpiWarps);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(d_full + b, 1);
+      mbar_init(d_empty + b, kWdEpiWarps);
+    }
     mbar_init(drain, 1);
     *abrt = 0;
     fence_mbar_init();
@@ -269,14 +276,15 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
     // one elected lane issues each tcgen05 instruction (and the commits, which track that lane's MMAs).
     uint32_t aslot = 0, aph = 0, bslot = 0, tc = 0;
     const uint64_t bdesc0 = sdesc_sw128(smem_u32(bring));
-    const uint32_t dcol = tmem + kWdDCol;
     bool ok = true;
     WD_PROF_T0(t_all);
     for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x, ++tc) {
       const WdTile t = wd_tile(i, tpre, offs, E, RB);
       const uint32_t idesc = idesc_bf16_m128(max(16, (t.n + 15) & ~15));
       WD_PROF_T0(t_d);
-      const bool d_ok = tc == 0 || wd_wait(d_empty, (tc + 1) & 1, abrt, p);  // epilogue drained the accumulator
+      const uint32_t db = tc & 1, dcol = tmem + kWdDCol + db * kWdTok;
+      // accumulator db was last used by tile tc - 2: its epilogue must have drained it
+      const bool d_ok = tc < 2 || wd_wait(d_empty + db, ((tc >> 1) + 1) & 1, abrt, p);
       if (!__all_sync(0xffffffffu, d_ok)) break;
       if (lane == 0) WD_PROF_ADD(2, t_d);
       if (lane == 0) WD_PROF_INC(12);
@@ -307,7 +315,7 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
         aph ^= (aslot == 0);
         bslot = bslot + 1 == (uint32_t)kWdBSt ? 0u : bslot + 1;
       }
-      if (ok && elect_one()) tc_commit(d_full);
+      if (ok && elect_one()) tc_commit(d_full + db);
       __syncwarp();
     }
     if (lane == 0) WD_PROF_ADD(3, t_all);
@@ -364,7 +372,8 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
       const WdTile t = wd_tile(i, tpre, offs, E, RB);
       const float gsc = p.gs[t.e] * kTwo52;  // loaded while the MMAs run
       WD_PROF_T0(t_d);
-      const bool good = wd_wait(d_full, tc & 1, abrt, p);
+      const uint32_t db = tc & 1;
+      const bool good = wd_wait(d_full + db, (tc >> 1) & 1, abrt, p);
       if (ew == 0 && lane == 0) WD_PROF_ADD(8, t_d);
       __syncwarp();
       (void)good;
@@ -375,7 +384,7 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
       for (int c0 = 128 * chalf; c0 < cend; c0 += 32) {
         uint32_t v[32];
         WD_PROF_T0(t_l);
-        tc_ld_x32(tmem + tlane + kWdDCol + c0, v);
+        tc_ld_x32(tmem + tlane + kWdDCol + db * kWdTok + c0, v);
         tc_wait_ld();
         if (ew == 0 && lane == 0) WD_PROF_ADD(14, t_l);
         WD_PROF_T0(t_m);
@@ -426,7 +435,7 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(d_empty);
+      if (lane == 0) mbar_arrive(d_empty + db);
     }
     if (ew == 0 && lane == 0) WD_PROF_ADD(9, t_all);
   }
