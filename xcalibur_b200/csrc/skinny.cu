@@ -17,11 +17,11 @@
 //   and no warp's slices straddle two units (DeepSeek-V3: 7 slices = 64.5 KB stages for gate_up, 4 for down).
 //   The CTA's down-projection weights are prefetched into L2 a piece per gate_up stage, so HBM sees one even
 //   stream and phase B reads L2 after the phase A -> B handoff.
-// * Partial sums leave the compute warps only at stage ends: each warp accumulates into one of two register
-//   sets, switches set at every flush point, and writes the finished set one stage later (its MMAs have long
-//   completed) or at the end of its segment, into a reduction slot.  Two epilogue warps consume the slots in order: they add the partials
-//   of each unit in warp order (deterministic) and apply the epilogue (SwiGLU -> inter, or y and the post-norm
-//   sums).
+// * Partial sums leave the compute warps only at stage ends: at every flush point a warp sums its accumulator's
+//   two chains into four pending partials and clears it, and writes the partials one stage later (or at the end
+//   of its segment) into a reduction slot; one accumulator set keeps a single copy of the unrolled hot loop per
+//   stage size.  Two epilogue warps consume the slots in order: they add the partials of each unit in warp order
+//   (deterministic) and apply the epilogue (SwiGLU -> inter, or y and the post-norm sums).
 // * Warp 17 stages each segment's activation rows (x for phase A, the job's SwiGLU output for phase B, after an
 //   acquire on that job's phase-A counter) with bulk copies and converts them to f16 in place; the epilogue warp
 //   that finishes a segment's last unit publishes it GPU-wide (one fence and one counter update per segment).
@@ -849,16 +849,18 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
   } else {
     // ------------------------------------------------------------------ compute warps
     // Stage i of a segment holds slices [i SS, i SS + ns); warp w takes [i SS + w PER, + PER), all in one unit.
-    // Two accumulator sets alternate at every flush point; the finished set is written one stage later.
+    // At a flush point the set's two chains are summed into four pending partials and the set is cleared; the
+    // partials are written one stage later (one hot-loop instantiation per stage size).
     const int g = lane >> 2, t = lane & 3;
     const bool wr = t < L.rl / 8;  // this lane's columns are read by the epilogue
-    int st = 0, f = 0, k = 0, cur = 0;
+    int st = 0, f = 0, k = 0;
     uint32_t sphase = 0;
     bool pend = false;
     int fpend = 0;
     float psc0 = 1.f, psc1 = 1.f;
-    float sa[2][4] = {}, sb[2][4] = {};  // the two accumulator sets, two chains each
-    auto deposit = [&](float (&c)[2][4]) {  // write a finished set into its slot and clear it
+    float sa[2][4] = {};                 // the accumulator set, two chains
+    float pv[4] = {0.f, 0.f, 0.f, 0.f};  // partials of the last flush, not yet written
+    auto deposit = [&]() {               // write the pending partials into their slot
       const int slot = fpend % SK_NSLOT;
       TRACE_T0(t_sf);
       if (fpend >= SK_NSLOT) mbar_wait(cb.slot_free + slot, ((fpend / SK_NSLOT) + 1) & 1, p.timeout_ns, status);
@@ -866,17 +868,9 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
         TRACE_SPAN(14, t_sf);
         TRACE_ADD(18, 1);
       }
-      if (wr) {
-        float v[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = c[0][i] + c[1][i];
+      if (wr)
         *reinterpret_cast<float4*>(red + slot * (L.red_slot / 4) + (warp * L.rl + t * 8 + g) * 4) =
-            make_float4(v[0] * psc0, v[1] * psc1, v[2] * psc0, v[3] * psc1);
-      }
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) c[j][i] = 0.f;
+            make_float4(pv[0] * psc0, pv[1] * psc1, pv[2] * psc0, pv[3] * psc1);
       __syncwarp();
       if (lane == 0) mbar_arrive(cb.slot_full + slot);
       pend = false;
@@ -916,10 +910,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
           const uint8_t* sl = ring + (size_t)st * L.slot_bytes + (size_t)warp * PER * SK_SLICE;
           const uint8_t* xs = xrow + (size_t)(my0 % U) * 128;
           TRACE_T0(t_c);
-          if (cur)
-            sk_run_per(PER, sl, xs, lane, t, sb);
-          else
-            sk_run_per(PER, sl, xs, lane, t, sa);
+          sk_run_per(PER, sl, xs, lane, t, sa);
           if (warp == 0) {
             __syncwarp();
             if (lane == 0) TRACE_SPAN(ph ? 31 : 23, t_c);
@@ -934,7 +925,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
         }
         if (pend) {
           TRACE_T0(t_d);
-          if (cur) deposit(sa); else deposit(sb);
+          deposit();
           if (warp == 0 && lane == 0) TRACE_SPAN(25, t_d);
         }
         if ((i + 1) % spe == 0) {
@@ -942,7 +933,12 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
           fpend = f++;
           psc0 = sc0;
           psc1 = sc1;
-          cur ^= 1;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            pv[i] = sa[0][i] + sa[1][i];
+            sa[0][i] = 0.f;
+            sa[1][i] = 0.f;
+          }
         }
         if (warp == 0 && lane == 0) TRACE_SPAN(ph ? 29 : 28, t_it);
       }
@@ -951,7 +947,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
       // the segment's last set is written now, not after the next segment's first stage: the next segment's
       // activations may wait (phase B) on phase-A counters that this very set completes
       if (pend) {
-        if (cur) deposit(sa); else deposit(sb);
+        deposit();
       }
       ++k;
     }
