@@ -41,7 +41,7 @@ CONFIGS = {
 METRIC = "MoE layer tokens/s; decode HBM GB/s & prefill TFLOPS vs B200 roofline"
 
 
-def config_for(name: str, experts: int = 0) -> dict:
+def config_for(name: str, experts: int = 0, tokens: int = 0) -> dict:
     if name.startswith("qwen"):
         T = int(name.split(":")[1]) if ":" in name else 64
         cfg = dict(workload=f"qwen3_30b_a3b_moe_T{T}", E=128, H=2048, I=768, T=T, k=8, bias_std=0.0)
@@ -51,6 +51,9 @@ def config_for(name: str, experts: int = 0) -> dict:
     if experts:
         cfg["E"] = experts
         cfg["workload"] += f"_E{experts}"
+    if tokens:
+        cfg["T"] = tokens
+        cfg["workload"] += f"_T{tokens}"
     return cfg
 
 
@@ -65,6 +68,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-tokens", type=int, default=1)
     ap.add_argument("--experts", type=int, default=0, help="override the expert count (small profiling cases)")
+    ap.add_argument("--tokens", type=int, default=0, help="override the token count (small profiling cases)")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
 
@@ -503,7 +507,7 @@ def run_reference(a, cfg):
 
 def main():
     a = parse()
-    cfg = config_for(a.config, a.experts)
+    cfg = config_for(a.config, a.experts, a.tokens)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if a.impl == "reference":
