@@ -158,6 +158,14 @@ int xcb_moe_read_status(void* workspace, int32_t* device_status, cudaStream_t st
 int xcb_hbm_probe(const void* src, size_t bytes, int mode, int chunk, int stages, int ctas_per_sm, int threads,
                   const long long* regions, int nreg, int32_t* status, float* sink, cudaStream_t stream);
 
+/* Tensor-pipe probe (diagnostic): one CTA per SM issues `chunks` x 4 back-to-back tcgen05.mma kind::f16
+ * (M = 128, N = n, K = 16; A from tensor memory, or shared memory with a_smem != 0), cycling four A and four B
+ * slots, with a tcgen05.commit after every `commit_every` chunks (a power of two; 0: none).  cycles[blockIdx]
+ * (device, one per SM)
+ * receives the clock cycles from the first issue to the completion of the last MMA. */
+int xcb_mma_probe(int a_smem, int n, int chunks, int commit_every, unsigned long long* cycles, int32_t* status,
+                  cudaStream_t stream);
+
 /* ---- expert parallelism ----
  * The reference models an expert-parallel rank only as a local expert range whose non-local routes are masked
  * (moe_w4a16.py:105-110, :513-520); the exchange between ranks was its harness's job.  These helpers give the

@@ -45,6 +45,7 @@ EXPORTS = (
     "xcb_moe_read_status",
     "xcb_nvfp4_quantize",
     "xcb_hbm_probe",
+    "xcb_mma_probe",
     "xcb_moe_topk",
     "xcb_ep_plan",
     "xcb_ep_gather",
@@ -98,6 +99,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "xcb_nvfp4_quantize": (ctypes.c_int, [P, I32, I32, I32, P, P, P, P, P]),
         "xcb_hbm_probe": (ctypes.c_int, [P, SZ, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                          P, ctypes.c_int, P, P, P]),
+        "xcb_mma_probe": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P]),
         "xcb_moe_topk": (ctypes.c_int, [P, I32, I32, I32, P, P, P]),
         "xcb_ep_plan": (ctypes.c_int, [P, I32, I32, I32, I32, P, P, P, P, P]),
         "xcb_ep_gather": (ctypes.c_int, [P, P, P, I32, I32, I32, I32, P, P, P, P, P, P]),
