@@ -15,8 +15,8 @@
 //   L2 evict-first).  A stage holds PER consecutive slices for each of the 16 compute warps, PER chosen per
 //   phase so that a unit (16 rows x the full reduction) either spans whole stages or a stage holds whole units
 //   and no warp's slices straddle two units (DeepSeek-V3: 7 slices = 64.5 KB stages for gate_up, 4 for down).
-//   The CTA's down-projection weights are prefetched into L2 a piece per gate_up stage, so HBM sees one even
-//   stream and phase B reads L2 after the phase A -> B handoff.
+//   Both phases stream from HBM: prefetching the down-projection weights into L2 during gate_up was measured
+//   slower (it delays the latency-critical gate_up stream more than phase B gains).
 // * Partial sums leave the compute warps only at stage ends: at every flush point a warp sums its accumulator's
 //   two chains into four pending partials and clears it, and writes the partials one stage later (or at the end
 //   of its segment) into a reduction slot; one accumulator set keeps a single copy of the unrolled hot loop per
@@ -77,7 +77,6 @@ constexpr int SK_NBUF_MAX = 2;                          // activation buffers
 constexpr int SK_SEG_RING = 64;                         // per-segment completion counters
 constexpr int SK_WARP_ROUTES = 32;                      // up to this many routes one warp builds the tables
 constexpr int SK_COPY_SPLIT = 36864;                    // stages above this many bytes go as two bulk copies
-constexpr long long SK_L2_PREFETCH_BYTES = 96ll << 20;  // phase-B weights up to this size are prefetched into L2
 constexpr int SK_SMEM_LIMIT = 227 * 1024;
 
 // Slices per warp per stage for a unit of U slices: U % PER == 0 (a warp's slices never straddle a unit) and
@@ -127,9 +126,6 @@ struct SkSegments {
     nj_0 = n[0]; nj_1 = n[1]; nj_2 = n[2]; nj_3 = n[3];
   }
   __device__ int count() const { return nj_0 + nj_1 + nj_2 + nj_3; }
-  __device__ int first_b() const { return nj_0 + nj_1; }  // index of the first phase-B segment
-  __device__ long long units_a() const { return u1_0 - u0_0 + u1_1 - u0_1; }
-  __device__ long long units_b() const { return u1_2 - u0_2 + u1_3 - u0_3; }
   // Segment i: phase, job, unit range [v0, v1).
   __device__ void at(int i, int& ph, int& job, long long& v0, long long& v1) const {
     int q = 0;
@@ -622,43 +618,11 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
       const uint64_t pol = policy_evict_first();
       int it = 0;
       bool ok = true;
-      // phase-B weights do not depend on phase A: when they fit in L2, this CTA's share is prefetched into L2 a
-      // piece per phase-A stage (so HBM sees one even stream) and phase B reads L2 after the A -> B handoff
-      const bool prefetch_b = (long long)njobs * nrbB * (long long)unitB <= SK_L2_PREFETCH_BYTES;
-      int pf_seg = segs.first_b();     // next phase-B segment to prefetch
-      size_t pf_off = 0;               // bytes of it already prefetched
-      size_t pf_step = 0;              // bytes per phase-A stage
-      if (prefetch_b && segs.first_b() > 0) {
-        // spread over the phase-A stages after the first ring fill (the first stages land sooner without it)
-        const long long nA = segs.units_a(), nB = segs.units_b();
-        long long stagesA = (nA * UA + 16 * L.perA - 1) / (16 * L.perA) + segs.first_b() - NST;
-        stagesA = stagesA < 1 ? 1 : stagesA;
-        pf_step = (size_t)((nB * (long long)unitB + stagesA - 1) / stagesA + 4095) & ~(size_t)4095;
-      }
-      auto prefetch_b_bytes = [&](size_t budget) {  // issue up to `budget` bytes of the remaining phase-B share
-        while (budget > 0 && pf_seg < nseg) {
-          int ph2, job2;
-          long long v0, v1;
-          segs.at(pf_seg, ph2, job2, v0, v1);
-          const size_t total = v1 > v0 ? (size_t)(v1 - v0) * unitB : 0;  // consecutive units are contiguous
-          if (pf_off >= total) {
-            ++pf_seg;
-            pf_off = 0;
-            continue;
-          }
-          const uint8_t* first = p.wB + ((size_t)jobs[job2].x * nrbB + (size_t)(v0 - (long long)job2 * nrbB)) * unitB;
-          const size_t n = min(min(total - pf_off, budget), (size_t)1 << 20);
-          bulk_prefetch_l2(first + pf_off, (uint32_t)n);
-          pf_off += n;
-          budget -= n;
-        }
-      };
       for (int s = 0; s < nseg && ok; ++s) {
         int ph, job;
         long long u0, u1;
         segs.at(s, ph, job, u0, u1);
         if (u1 <= u0) continue;
-        if (ph == 1 && prefetch_b) prefetch_b_bytes((size_t)-1);  // whatever phase A did not cover
         const int nrb = ph ? nrbB : nrbA, U = ph ? UB : UA, SS = 16 * (ph ? L.perB : L.perA);
         const int nsl = (int)(u1 - u0) * U;
         const uint8_t* seg = (ph ? p.wB : p.wA) +
@@ -682,7 +646,6 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
           } else {
             bulk_g2s_stream(dst, src, bytes, cb.full + st, pol);
           }
-          if (ph == 0 && prefetch_b && it >= NST) prefetch_b_bytes(pf_step);
         }
       }
       TRACE_AT(3);
