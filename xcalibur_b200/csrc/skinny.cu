@@ -115,8 +115,13 @@ struct SkSegments {
       const int nrb = ph ? nrbB : nrbA;
       const int j0 = w < W ? njobs * w / W : njobs, j1 = w < W ? njobs * (w + 1) / W : njobs;
       const long long cnt = (long long)(j1 - j0) * nrb;
-      a[q] = (long long)j0 * nrb + cnt * bid / G;
-      b[q] = (long long)j0 * nrb + cnt * (bid + 1) / G;
+      // the share a CTA takes differs per sequence (a bijection of the CTA index: 41 is prime, so coprime with G
+      // unless G is a multiple of it): a CTA whose share of one sequence streams slowly (the slow part of the
+      // address space) gets other parts of the others, which evens the CTAs' finish times (measured 1.5 %)
+      const int mul = G % 41 ? 41 : 1;
+      const int sb = (int)(((long long)bid * mul + q * 17) % G);
+      a[q] = (long long)j0 * nrb + cnt * sb / G;
+      b[q] = (long long)j0 * nrb + cnt * (sb + 1) / G;
       f[q] = (int)(a[q] / nrb);
       n[q] = b[q] > a[q] ? (int)((b[q] - 1) / nrb) - f[q] + 1 : 0;
     }
