@@ -359,6 +359,8 @@ def run_xcb_ep(a, cfg, rank, world, dist):
     if graph is not None:
         del graph  # a graph holding NCCL calls must be released before the process group is destroyed
         torch.cuda.synchronize()
+    dense_p2p = T <= ExpertParallelMoE.DENSE_MAX_TOKENS and layer.p2p is not None
+    layer.close()  # the peer exchange's buffers (collective)
     u_avg = sum(U[i % P] for i in range(K)) / K
     r_avg = sum(R[i % P] for i in range(K)) / K
     res = finish(a, cfg, world, ms, ms, e2e_ms, u_avg, P, clk, None)
@@ -375,12 +377,20 @@ def run_xcb_ep(a, cfg, rank, world, dist):
     res["roofline"]["step_ms"] = round(ms, 5)
     res["config"]["parallelism"] = f"ep{world}"
     res["config"]["step_launch"] = "one CUDA graph replay per step" if T <= 32 else "eager (planned exchange)"
+    res["config"]["exchange"] = ("NVLink peer memory (dispatch/combine kernels)" if dense_p2p else
+                                 "NCCL all-to-all" if T <= 32 else "NCCL all-to-all (planned, uneven splits)")
     res["config"]["experts_per_gpu"] = epr
     res["config"]["l2"] = (f"{P} rotating inputs per rank; {u_avg:.1f} distinct local experts and {r_avg:.0f} local "
                            f"routes per rank per step")
     # per step: top-k, plan, gather, combine + the local layer (one decode launch, or router + gather + two grouped
     # GEMMs + combine on the prefill path)
-    res["gpu_launches"] = K * (4 + (1 if T * k <= 256 else 5))
+    # this library's kernels per step: router top-k, then the exchange (peer dispatch + combine; or NCCL with the
+    # combine kernel; or plan + gather + combine), and the local layer (one launch up to 256 local routes, else 5)
+    local = 1 if world * T * k <= 256 else 5
+    if T <= ExpertParallelMoE.DENSE_MAX_TOKENS:
+        res["gpu_launches"] = K * ((3 if dense_p2p else 2) + local)
+    else:
+        res["gpu_launches"] = K * (4 + local)
     return res
 
 

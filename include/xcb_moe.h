@@ -195,6 +195,27 @@ int xcb_ep_gather(const uint16_t* x, const int32_t* ids, const float* wts, int32
 int xcb_ep_combine(const uint16_t* parts, const int32_t* counts, const int32_t* send_pos, int32_t T, int32_t H,
                    int32_t G, uint16_t* out, cudaStream_t stream);
 
+/* Peer exchange for small batches (every rank sends the same T <= T_max tokens to every rank), over NVLink peer
+ * memory instead of a collective library.  Each rank allocates one buffer of xcb_ep_p2p_bytes() with
+ * xcb_p2p_alloc (zeroed; handle = 64-byte CUDA IPC handle to share with the other ranks), opens the others'
+ * with xcb_p2p_open, and passes peers = device uint64 [G] (peers[d] = rank d's buffer in this process, peers[rank]
+ * its own).  Layout of a buffer for a step of T tokens: x bf16 [G * T, H] (row d*T + t = token t of rank d),
+ * meta int32 [G * T, 2k] (k ids, then k fp32 weight bit patterns), partial sums bf16 [G * T, H], flags.
+ * xcb_ep_p2p_dispatch writes this rank's rows into every buffer and returns once (in stream order) every rank's
+ * rows are in this rank's buffer; the local layer then runs on them; xcb_ep_p2p_combine sends partial rows
+ * [d*T, (d+1)*T) to rank d and writes out bf16 [T, H] = sum over source ranks in rank order.  Every rank must make
+ * the same calls in the same order.  Waits are bounded (2 s): status gets XCB_STATUS_DEVICE_TIMEOUT. */
+size_t xcb_ep_p2p_bytes(int32_t G, int32_t T_max, int32_t H, int32_t k);
+int xcb_p2p_alloc(size_t bytes, void** ptr, void* handle);
+int xcb_p2p_open(const void* handle, void** ptr);
+int xcb_p2p_close(void* ptr);
+int xcb_p2p_free(void* ptr);
+int xcb_ep_p2p_dispatch(const uint16_t* x, const int32_t* ids, const float* wts, int32_t T, int32_t T_max, int32_t H,
+                        int32_t k, int32_t G, int32_t rank, const uint64_t* peers, int32_t* status,
+                        cudaStream_t stream);
+int xcb_ep_p2p_combine(const uint16_t* parts, int32_t T, int32_t T_max, int32_t H, int32_t k, int32_t G,
+                       int32_t rank, const uint64_t* peers, uint16_t* out, int32_t* status, cudaStream_t stream);
+
 /* Quantise fp32 weights [E, R, K] to NVFP4 (gs = amax/(6*448) per expert, sf = e4m3(block_amax/6/gs),
  * codes RNE to E2M1): codes [E, R, K/2], sf [E, R, K/16], gs [E].  A utility for synthetic weights; the
  * reference receives already-quantised weights.  amax_scratch: device float [E] (zeroed by this call). */

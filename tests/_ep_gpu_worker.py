@@ -9,7 +9,7 @@ import torch
 import torch.distributed as dist
 
 
-def nccl_worker(rank, world, port, E, H, I, T, k, seed, result_dir):
+def nccl_worker(rank, world, port, E, H, I, T, k, seed, result_dir, p2p=True, calls=1):
     from xcalibur_b200 import PreparedMoE, synth
     from xcalibur_b200.ep import ExpertParallelMoE
 
@@ -18,20 +18,27 @@ def nccl_worker(rank, world, port, E, H, I, T, k, seed, result_dir):
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    ep = None
     try:
         w = synth.make_weights(E, H, I, seed=seed, device=dev)           # the whole layer, same on every rank
         epr = E // world
         shard = {n: t[rank * epr:(rank + 1) * epr].contiguous() for n, t in w.items()}
-        ep = ExpertParallelMoE(*shard.values(), total_experts=E)
+        ep = ExpertParallelMoE(*shard.values(), total_experts=E, top_k=k, p2p=p2p)
         full = PreparedMoE(*w.values())
-        x, logits = synth.make_inputs(T, H, E, seed=seed + 1 + rank, device=dev, bias_std=0.5)
-        out_ep = ep.forward(x, logits, k)
-        out_1 = full.forward(x, logits, k)
+        got, want = [], []
+        for c in range(calls):  # consecutive calls: the peer exchange's per-step flags must advance in step
+            x, logits = synth.make_inputs(T, H, E, seed=seed + 1 + rank + 100 * c, device=dev, bias_std=0.5)
+            got.append(ep.forward(x, logits, k))
+            want.append(full.forward(x, logits, k))
         torch.cuda.synchronize()
         st = ep.ops.device_status() | ep.ops.layer.check_device_status() | full.check_device_status()
+        if ep.p2p is not None:
+            st |= ep.p2p.device_status()
         np.save(os.path.join(result_dir, f"nccl_{rank}.npy"),
-                np.stack([out_ep.view(torch.int16).cpu().numpy().view(np.uint16),
-                          out_1.view(torch.int16).cpu().numpy().view(np.uint16)]))
+                np.stack([torch.cat(got).view(torch.int16).cpu().numpy().view(np.uint16),
+                          torch.cat(want).view(torch.int16).cpu().numpy().view(np.uint16)]))
         np.save(os.path.join(result_dir, f"nccl_status_{rank}.npy"), np.array([st]))
     finally:
+        if ep is not None:
+            ep.close()
         dist.destroy_process_group()

@@ -1,4 +1,5 @@
-"""Expert parallelism on two GPUs over NCCL: each rank's output equals a single-GPU layer holding every expert."""
+"""Expert parallelism on two GPUs (NVLink peer exchange and NCCL): each rank's output equals a single-GPU layer
+holding every expert."""
 import os
 import socket
 
@@ -19,12 +20,15 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("T", [1, 600])  # dense exchange, planned exchange
-def test_ep_two_gpus_match_single_gpu(tmp_path, T):
+@pytest.mark.parametrize("T,p2p,calls", [(1, True, 3), (7, True, 2), (1, False, 1), (600, True, 1)])
+def test_ep_two_gpus_match_single_gpu(tmp_path, T, p2p, calls):
+    """Dense exchange over NVLink peer memory (several consecutive steps), dense exchange over NCCL, planned
+    exchange over NCCL."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world, E, H, I, k = 2, 32, 2048, 768, 8
-    mp.spawn(nccl_worker, args=(world, _free_port(), E, H, I, T, k, 77, str(tmp_path)), nprocs=world, join=True)
+    mp.spawn(nccl_worker, args=(world, _free_port(), E, H, I, T, k, 77, str(tmp_path), p2p, calls), nprocs=world,
+             join=True)
     for r in range(world):
         assert int(np.load(os.path.join(tmp_path, f"nccl_status_{r}.npy"))[0]) == 0
         got, want = np.load(os.path.join(tmp_path, f"nccl_{r}.npy"))

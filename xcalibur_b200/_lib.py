@@ -49,6 +49,13 @@ EXPORTS = (
     "xcb_moe_topk",
     "xcb_ep_plan",
     "xcb_ep_gather",
+    "xcb_ep_p2p_bytes",
+    "xcb_p2p_alloc",
+    "xcb_p2p_open",
+    "xcb_p2p_close",
+    "xcb_p2p_free",
+    "xcb_ep_p2p_dispatch",
+    "xcb_ep_p2p_combine",
     "xcb_ep_combine",
 )
 
@@ -102,6 +109,13 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "xcb_mma_probe": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P]),
         "xcb_moe_topk": (ctypes.c_int, [P, I32, I32, I32, P, P, P]),
         "xcb_ep_plan": (ctypes.c_int, [P, I32, I32, I32, I32, P, P, P, P, P]),
+        "xcb_ep_p2p_bytes": (SZ, [I32, I32, I32, I32]),
+        "xcb_p2p_alloc": (ctypes.c_int, [SZ, ctypes.POINTER(ctypes.c_void_p), P]),
+        "xcb_p2p_open": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_void_p)]),
+        "xcb_p2p_close": (ctypes.c_int, [P]),
+        "xcb_p2p_free": (ctypes.c_int, [P]),
+        "xcb_ep_p2p_dispatch": (ctypes.c_int, [P, P, P, I32, I32, I32, I32, I32, I32, P, P, P]),
+        "xcb_ep_p2p_combine": (ctypes.c_int, [P, I32, I32, I32, I32, I32, I32, P, P, P, P]),
         "xcb_ep_gather": (ctypes.c_int, [P, P, P, I32, I32, I32, I32, P, P, P, P, P, P]),
         "xcb_ep_combine": (ctypes.c_int, [P, P, P, I32, I32, I32, P, P]),
     }

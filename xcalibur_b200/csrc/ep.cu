@@ -9,6 +9,8 @@
 //   gather   destination-major send rows: x[send_tok[d][i]] with the token's full top-k ids and weights (the
 //            receiving rank masks the experts it does not hold);
 //   combine  out[t] = bf16(sum over ranks d, in rank order, of the partial returned for (t, d)).
+#include <cstring>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -212,6 +214,218 @@ int xcb_ep_combine(const uint16_t* parts, const int32_t* counts, const int32_t* 
   const int sms = ep_sm_count();
   if (!sms) return XCB_ERR_CUDA;
   ep_combine_kernel<<<sms * 4, 256, 0, stream>>>(parts, counts, send_pos, T, H, G, out);
+  return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------------------------------------ peer exchange
+// Dense exchange for small batches over NVLink peer memory, without NCCL: every rank holds one buffer (same layout
+// on every rank, mapped into every peer through CUDA IPC) with, per source rank d, a slot for d's token rows and
+// their top-k row (written by d) and a slot for the partial sums this rank's tokens got on d (written by d).
+// dispatch: push this rank's rows into slot [rank] of every peer, fence, raise the peer's x flag; wait until every
+// peer has raised this rank's.  combine: push each peer's partial rows into slot [rank] of that peer, fence, raise
+// its part flag; wait for all; out = bf16(sum over d in rank order).  Flags count block arrivals and only grow
+// (epoch e of this rank: e * blocks per peer), so no reset is needed between steps; every wait is bounded.
+namespace xcb {
+
+struct P2pLayout {
+  size_t x, meta, part, flag, total;
+};
+__host__ __device__ inline P2pLayout p2p_layout(int G, int Tm, int H, int k) {
+  P2pLayout L;
+  size_t o = 0;
+  auto take = [&](size_t b) { size_t at = o; o = (o + b + 255) / 256 * 256; return at; };
+  L.x = take((size_t)G * Tm * H * 2);
+  L.meta = take((size_t)G * Tm * 2 * k * 4);
+  L.part = take((size_t)G * Tm * H * 2);
+  L.flag = take((size_t)(2 * G + 4) * 4);  // x flags [G], part flags [G], epoch, block counter
+  L.total = o;
+  return L;
+}
+
+constexpr int kP2pRowBytesPerBlock = 65536;  // rows per pushing block: about 64 KB
+
+__device__ __forceinline__ unsigned p2p_load_acquire(const unsigned* a) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void p2p_red_release(unsigned* a, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+
+// Wait (bounded) until every flag [0, G) of `flags` reaches `target`; false on timeout (status bit set).
+__device__ bool p2p_wait_all(const unsigned* flags, int G, unsigned target, uint64_t timeout_ns, int* status) {
+  const uint64_t t0 = gtimer();
+  for (int d = 0; d < G; ++d) {
+    while ((int)(p2p_load_acquire(flags + d) - target) < 0) {
+      __nanosleep(64);
+      if (gtimer() - t0 > timeout_ns) {
+        set_status(status, XCB_STATUS_DEVICE_TIMEOUT);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+__global__ void ep_p2p_dispatch_kernel(const uint16_t* __restrict__ x, const int* __restrict__ ids,
+                                       const float* __restrict__ wts, int T, int Tm, int H, int k, int G, int rank,
+                                       const uint64_t* __restrict__ peers, int nb, P2pLayout L, uint64_t timeout_ns,
+                                       int* status) {
+  (void)Tm;
+  const int d = blockIdx.x / nb, sub = blockIdx.x % nb;
+  uint8_t* mine = reinterpret_cast<uint8_t*>(peers[rank]);
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(mine + L.flag + 2 * G * 4) + 1;  // this step's epoch
+  uint8_t* dst = reinterpret_cast<uint8_t*>(peers[d]);
+  const int r0 = T * sub / nb, r1 = T * (sub + 1) / nb;
+  const int nv = H / 8;
+  const uint4* src = reinterpret_cast<const uint4*>(x);
+  // slots are T rows apart (every rank sends T rows this step), so the received rows form one [G T, H] matrix
+  uint4* dx = reinterpret_cast<uint4*>(dst + L.x + (size_t)rank * T * H * 2);
+  for (int i = r0 * nv + threadIdx.x; i < r1 * nv; i += blockDim.x) dx[i] = __ldg(src + i);
+  int* dm = reinterpret_cast<int*>(dst + L.meta + (size_t)rank * T * 2 * k * 4);
+  for (int i = r0 * k + threadIdx.x; i < r1 * k; i += blockDim.x) {
+    const int t = i / k, s = i % k;
+    dm[t * 2 * k + s] = ids[i];
+    dm[t * 2 * k + k + s] = __float_as_int(wts[i]);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) p2p_red_release(reinterpret_cast<unsigned*>(dst + L.flag) + rank, 1u);
+  // one block waits for every peer's rows in this rank's buffer; the kernels after this one read them
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    p2p_wait_all(reinterpret_cast<const unsigned*>(mine + L.flag), G, e * (unsigned)nb, timeout_ns, status);
+    __threadfence_system();
+  }
+}
+
+__global__ void ep_p2p_combine_kernel(const uint16_t* __restrict__ parts, int T, int Tm, int H, int G, int rank,
+                                      const uint64_t* __restrict__ peers, int nb, P2pLayout L, uint16_t* __restrict__ out,
+                                      uint64_t timeout_ns, int* status) {
+  (void)Tm;
+  const int d = blockIdx.x / nb, sub = blockIdx.x % nb;
+  uint8_t* mine = reinterpret_cast<uint8_t*>(peers[rank]);
+  unsigned* epoch = reinterpret_cast<unsigned*>(mine + L.flag + 2 * G * 4);
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(epoch) + 1;
+  uint8_t* dst = reinterpret_cast<uint8_t*>(peers[d]);
+  const int r0 = T * sub / nb, r1 = T * (sub + 1) / nb;
+  const int nv = H / 8;
+  // rank d's tokens are rows [d T, (d + 1) T) of this rank's partial sums
+  const uint4* src = reinterpret_cast<const uint4*>(parts + (size_t)d * T * H);
+  uint4* dp = reinterpret_cast<uint4*>(dst + L.part + (size_t)rank * T * H * 2);
+  for (int i = r0 * nv + threadIdx.x; i < r1 * nv; i += blockDim.x) dp[i] = __ldg(src + i);
+  __threadfence_system();
+  __syncthreads();
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    p2p_red_release(reinterpret_cast<unsigned*>(dst + L.flag) + G + rank, 1u);
+    ok = p2p_wait_all(reinterpret_cast<const unsigned*>(mine + L.flag) + G, G, e * (unsigned)nb, timeout_ns, status);
+  }
+  __syncthreads();
+  if (ok) {
+    // out = bf16(sum over source ranks in rank order), this block's slice of the T x H outputs
+    const uint16_t* pin = reinterpret_cast<const uint16_t*>(mine + L.part);
+    const int nq = T * (H / 4);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nq; i += gridDim.x * blockDim.x) {
+      const int t = i / (H / 4), c = (i % (H / 4)) * 4;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      for (int s = 0; s < G; ++s) {
+        const uint2 v = __ldcv(reinterpret_cast<const uint2*>(pin + ((size_t)s * T + t) * H + c));
+        a0 += bf2f((uint16_t)(v.x & 0xFFFFu));
+        a1 += bf2f((uint16_t)(v.x >> 16));
+        a2 += bf2f((uint16_t)(v.y & 0xFFFFu));
+        a3 += bf2f((uint16_t)(v.y >> 16));
+      }
+      uint2 o;
+      o.x = (uint32_t)f2bf(a0) | ((uint32_t)f2bf(a1) << 16);
+      o.y = (uint32_t)f2bf(a2) | ((uint32_t)f2bf(a3) << 16);
+      *reinterpret_cast<uint2*>(out + (size_t)t * H + c) = o;
+    }
+  }
+  // the last block to finish advances this rank's epoch (every block has read it by then)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned* cnt = epoch + 1;
+    __threadfence();
+    if (atomicAdd(cnt, 1u) == gridDim.x - 1) {
+      *cnt = 0;
+      *epoch = e;
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace xcb
+
+extern "C" {
+
+size_t xcb_ep_p2p_bytes(int32_t G, int32_t T_max, int32_t H, int32_t k) {
+  if (G <= 0 || G > kEpMaxRanks || T_max <= 0 || H <= 0 || k <= 0) return 0;
+  return p2p_layout(G, T_max, H, k).total;
+}
+
+int xcb_p2p_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return XCB_ERR_INVALID_ARG;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return XCB_ERR_CUDA;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess ||
+      cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle), p) != cudaSuccess) {
+    cudaFree(p);
+    return XCB_ERR_CUDA;
+  }
+  *ptr = p;
+  return XCB_OK;
+}
+
+int xcb_p2p_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return XCB_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
+}
+
+int xcb_p2p_close(void* ptr) {
+  if (!ptr) return XCB_ERR_INVALID_ARG;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
+}
+
+int xcb_p2p_free(void* ptr) {
+  if (!ptr) return XCB_ERR_INVALID_ARG;
+  return cudaFree(ptr) == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
+}
+
+static int p2p_blocks(int T, int H) {
+  const long long bytes = (long long)T * H * 2;
+  long long nb = (bytes + kP2pRowBytesPerBlock - 1) / kP2pRowBytesPerBlock;
+  nb = nb < 1 ? 1 : nb;
+  return (int)(nb > T ? T : nb);
+}
+
+int xcb_ep_p2p_dispatch(const uint16_t* x, const int32_t* ids, const float* wts, int32_t T, int32_t T_max, int32_t H,
+                        int32_t k, int32_t G, int32_t rank, const uint64_t* peers, int32_t* status,
+                        cudaStream_t stream) {
+  if (T <= 0 || T > T_max || H <= 0 || H % 8 || k <= 0 || k > 16 || G <= 0 || G > kEpMaxRanks || rank < 0 ||
+      rank >= G)
+    return XCB_ERR_INVALID_ARG;
+  if (!x || !ids || !wts || !peers || !status || ((uintptr_t)x & 15u)) return XCB_ERR_INVALID_ARG;
+  const int nb = p2p_blocks(T, H);
+  ep_p2p_dispatch_kernel<<<G * nb, 256, 0, stream>>>(x, ids, wts, T, T_max, H, k, G, rank, peers, nb,
+                                                     p2p_layout(G, T_max, H, k), 2000000000ull, status);
+  return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
+}
+
+int xcb_ep_p2p_combine(const uint16_t* parts, int32_t T, int32_t T_max, int32_t H, int32_t k, int32_t G,
+                       int32_t rank, const uint64_t* peers, uint16_t* out, int32_t* status, cudaStream_t stream) {
+  if (T <= 0 || T > T_max || H <= 0 || H % 8 || k <= 0 || k > 16 || G <= 0 || G > kEpMaxRanks || rank < 0 ||
+      rank >= G)
+    return XCB_ERR_INVALID_ARG;
+  if (!parts || !peers || !out || !status || ((uintptr_t)parts & 15u) || ((uintptr_t)out & 7u))
+    return XCB_ERR_INVALID_ARG;
+  const int nb = p2p_blocks(T, H);
+  ep_p2p_combine_kernel<<<G * nb, 256, 0, stream>>>(parts, T, T_max, H, G, rank, peers, nb,
+                                                    p2p_layout(G, T_max, H, k), out, 2000000000ull, status);
   return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
 }
 

@@ -14,13 +14,18 @@ is, on every rank (``forward``):
 5. all-to-all back in the same order, then ``xcb_ep_combine``: out[t] = bf16(sum of its partials in rank order).
 
 Small batches (at most DENSE_MAX_TOKENS tokens per rank, decode) skip the plan: every token goes to every rank with
-equal splits, so the step has three collectives and no host synchronisation.
+equal splits and no host synchronisation.  On GPUs that exchange runs over NVLink peer memory (``P2PExchange``:
+one buffer per rank mapped into every peer through CUDA IPC; a dispatch kernel writes this rank's rows into every
+peer and waits for theirs, a combine kernel returns the partial sums and adds them in rank order), so a decode step
+needs no collective library call; elsewhere it is three all-to-alls.
 
 The transport is ``torch.distributed.all_to_all_single`` (NCCL over NVLink on GPUs).  The per-rank steps run in the
 C-ABI library; ``_ops`` exists so that tests can substitute a CPU model of those steps and check the exchange
 protocol itself with the gloo backend (world size 2) on machines without GPUs.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -31,6 +36,107 @@ from .moe import PreparedMoE
 
 def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def p2p_layout(G: int, T_max: int, H: int, k: int):
+    """Byte offsets (x, meta, part, flag) and total size of a peer-exchange buffer (mirrors the C library's)."""
+    o = 0
+
+    def take(b):
+        nonlocal o
+        at = o
+        o = (o + b + 255) // 256 * 256
+        return at
+
+    x = take(G * T_max * H * 2)
+    meta = take(G * T_max * 2 * k * 4)
+    part = take(G * T_max * H * 2)
+    flag = take((2 * G + 4) * 4)
+    return x, meta, part, flag, o
+
+
+class _DeviceBytes:
+    """A device allocation seen by torch as a uint8 tensor (zero-copy, through the CUDA array interface)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+class P2PExchange:
+    """This rank's end of the NVLink peer exchange of the dense (small-batch) expert-parallel step.
+
+    Collective: every rank of ``group`` constructs it (the buffers' IPC handles are exchanged) and must ``close`` it
+    before the process group is destroyed."""
+
+    def __init__(self, lib, group, rank: int, world: int, T_max: int, H: int, k: int, device):
+        self.lib, self.group, self.rank, self.world = lib, group, rank, world
+        self.T_max, self.H, self.k, self.device = T_max, H, k, device
+        self.offs = p2p_layout(world, T_max, H, k)
+        nbytes = int(lib.xcb_ep_p2p_bytes(world, T_max, H, k))
+        if nbytes != self.offs[4]:
+            raise RuntimeError("peer-exchange layout mismatch between the library and its Python mirror")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        check(lib.xcb_p2p_alloc(nbytes, ctypes.byref(own), handle), "xcb_p2p_alloc")
+        self.own = own.value
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.opened = []
+        ptrs = []
+        for d in range(world):
+            if d == rank:
+                ptrs.append(self.own)
+                continue
+            h = (ctypes.c_ubyte * 64).from_buffer_copy(handles[d])
+            p = ctypes.c_void_p()
+            check(lib.xcb_p2p_open(h, ctypes.byref(p)), "xcb_p2p_open")
+            self.opened.append(p.value)
+            ptrs.append(p.value)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        self.buf = torch.as_tensor(_DeviceBytes(self.own, nbytes), device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def recv(self, T: int):
+        """This step's received rows: x bf16 [G T, H], ids int32 [G T, k], weights fp32 [G T, k] (views/copies)."""
+        G, H, k = self.world, self.H, self.k
+        xo, mo = self.offs[0], self.offs[1]
+        xr = self.buf[xo:xo + G * T * H * 2].view(torch.bfloat16).view(G * T, H)
+        meta = self.buf[mo:mo + G * T * 2 * k * 4].view(torch.int32).view(G * T, 2 * k)
+        return xr, meta[:, :k].contiguous(), meta[:, k:].contiguous().view(torch.float32)
+
+    def dispatch(self, x, ids, wts):
+        T = x.shape[0]
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        check(self.lib.xcb_ep_p2p_dispatch(x.data_ptr(), ids.data_ptr(), wts.data_ptr(), T, self.T_max, self.H,
+                                           self.k, self.world, self.rank, self.peers.data_ptr(),
+                                           self.status.data_ptr(), stream), "xcb_ep_p2p_dispatch")
+
+    def combine(self, parts, T: int):
+        out = torch.empty((T, self.H), dtype=torch.bfloat16, device=self.device)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        check(self.lib.xcb_ep_p2p_combine(parts.data_ptr(), T, self.T_max, self.H, self.k, self.world, self.rank,
+                                          self.peers.data_ptr(), out.data_ptr(), self.status.data_ptr(), stream),
+              "xcb_ep_p2p_combine")
+        return out
+
+    def device_status(self) -> int:
+        v = int(self.status.item())
+        self.status.zero_()
+        return v
+
+    def close(self):
+        """Unmap the peers' buffers, wait for every rank to do the same, free this rank's (collective)."""
+        if self.own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        for p in self.opened:
+            self.lib.xcb_p2p_close(p)
+        self.opened = []
+        dist.barrier(group=self.group)
+        self.buf = None
+        self.lib.xcb_p2p_free(self.own)
+        self.own = None
 
 
 class CudaEpOps:
@@ -101,7 +207,7 @@ class ExpertParallelMoE:
     ``moe_w4a16.py:72-79``); every rank of ``group`` calls ``forward`` with its own tokens, collectively."""
 
     def __init__(self, w13, w13_sf, w13_gs, w2, w2_sf, w2_gs, *, total_experts: int, group=None,
-                 post_norm_w=None, _ops=None):
+                 post_norm_w=None, top_k: int = 8, p2p: bool = True, _ops=None):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -118,6 +224,18 @@ class ExpertParallelMoE:
             _ops = CudaEpOps(layer)
         self.ops = _ops
         self.last = {}
+        # dense steps over NVLink peer memory (GPU ranks only; collective construction)
+        self.p2p = None
+        if p2p and isinstance(_ops, CudaEpOps) and self.world > 1:
+            H = w13.shape[2] * 2
+            self.p2p = P2PExchange(_ops.lib, group, self.rank, self.world, self.DENSE_MAX_TOKENS, H, top_k,
+                                   _ops.device)
+
+    def close(self):
+        """Release the peer exchange (collective; before the process group is destroyed)."""
+        if self.p2p is not None:
+            self.p2p.close()
+            self.p2p = None
 
     def _a2a(self, send: torch.Tensor, send_splits, recv_splits, trailing) -> torch.Tensor:
         out = torch.empty((sum(recv_splits), *trailing), dtype=send.dtype, device=send.device)
@@ -129,6 +247,17 @@ class ExpertParallelMoE:
     # splits), so no counts exchange and no host synchronisation are needed; a rank holding none of a token's experts
     # returns a zero partial for it.  Small batches (decode) are latency-bound, and this halves their collectives.
     DENSE_MAX_TOKENS = 32
+
+    def _dense_p2p(self, x, ids, wts, top_k):
+        T = x.shape[0]
+        ex = self.p2p
+        ex.dispatch(x, ids, wts)
+        xr, ids_r, w_r = ex.recv(T)
+        parts = self.ops.local(xr, ids_r, w_r, self.post_norm)
+        out = ex.combine(parts, T)
+        self.last.update({"ids": ids, "wts": wts, "send": [T] * self.world, "recv": [T] * self.world,
+                          "recv_ids": ids_r})
+        return out
 
     def _dense(self, x, ids, wts, top_k):
         T, H = x.shape
@@ -164,6 +293,8 @@ class ExpertParallelMoE:
             raise ValueError(f"router_logits must be [T, {self.E}]")
         ids, wts = self.ops.topk(router_logits, top_k)
         if 0 < T <= self.DENSE_MAX_TOKENS:
+            if self.p2p is not None and top_k == self.p2p.k:
+                return self._dense_p2p(x, ids, wts, top_k)
             return self._dense(x, ids, wts, top_k)
         counts, send_tok, send_pos = self.ops.plan(ids, self.epr, self.world)
         recv_counts = torch.empty_like(counts)
