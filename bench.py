@@ -360,6 +360,7 @@ def run_xcb_ep(a, cfg, rank, world, dist):
         del graph  # a graph holding NCCL calls must be released before the process group is destroyed
         torch.cuda.synchronize()
     dense_p2p = T <= ExpertParallelMoE.DENSE_MAX_TOKENS and layer.p2p is not None
+    p2p_error = layer.p2p_error
     layer.close()  # the peer exchange's buffers (collective)
     u_avg = sum(U[i % P] for i in range(K)) / K
     r_avg = sum(R[i % P] for i in range(K)) / K
@@ -379,6 +380,8 @@ def run_xcb_ep(a, cfg, rank, world, dist):
     res["config"]["step_launch"] = "one CUDA graph replay per step" if T <= 32 else "eager (planned exchange)"
     res["config"]["exchange"] = ("NVLink peer memory (dispatch/combine kernels)" if dense_p2p else
                                  "NCCL all-to-all" if T <= 32 else "NCCL all-to-all (planned, uneven splits)")
+    if p2p_error:
+        res["config"]["exchange"] += f" (peer exchange unavailable: {p2p_error})"
     res["config"]["experts_per_gpu"] = epr
     res["config"]["l2"] = (f"{P} rotating inputs per rank; {u_avg:.1f} distinct local experts and {r_avg:.0f} local "
                            f"routes per rank per step")

@@ -63,11 +63,16 @@ class _DeviceBytes:
                                          "strides": None}
 
 
+class P2PUnavailable(RuntimeError):
+    """The peer exchange could not be set up on every rank (mapping or self-test failed); all ranks agree on it."""
+
+
 class P2PExchange:
     """This rank's end of the NVLink peer exchange of the dense (small-batch) expert-parallel step.
 
-    Collective: every rank of ``group`` constructs it (the buffers' IPC handles are exchanged) and must ``close`` it
-    before the process group is destroyed."""
+    Collective: every rank of ``group`` constructs it (the buffers' IPC handles are exchanged, every rank's mapping
+    and a one-step self-test are checked by all ranks together) and must ``close`` it before the process group is
+    destroyed.  Raises ``P2PUnavailable`` on every rank if any rank failed, after releasing what it set up."""
 
     def __init__(self, lib, group, rank: int, world: int, T_max: int, H: int, k: int, device):
         self.lib, self.group, self.rank, self.world = lib, group, rank, world
@@ -84,18 +89,71 @@ class P2PExchange:
         dist.all_gather_object(handles, bytes(handle), group=group)
         self.opened = []
         ptrs = []
-        for d in range(world):
-            if d == rank:
-                ptrs.append(self.own)
-                continue
-            h = (ctypes.c_ubyte * 64).from_buffer_copy(handles[d])
-            p = ctypes.c_void_p()
-            check(lib.xcb_p2p_open(h, ctypes.byref(p)), "xcb_p2p_open")
-            self.opened.append(p.value)
-            ptrs.append(p.value)
+        why = ""
+        try:
+            for d in range(world):
+                if d == rank:
+                    ptrs.append(self.own)
+                    continue
+                h = (ctypes.c_ubyte * 64).from_buffer_copy(handles[d])
+                p = ctypes.c_void_p()
+                check(lib.xcb_p2p_open(h, ctypes.byref(p)), "xcb_p2p_open")
+                self.opened.append(p.value)
+                ptrs.append(p.value)
+        except Exception as e:  # noqa: BLE001 - reported to every rank below
+            why = f"rank {rank}: {e}"
+        if not self._agree(not why):
+            self.close()
+            raise P2PUnavailable(why or "another rank could not map the peer buffers")
         self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
         self.buf = torch.as_tensor(_DeviceBytes(self.own, nbytes), device=device)
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        why = self._self_test()
+        if not self._agree(not why):
+            self.close()
+            raise P2PUnavailable(why or "the self-test failed on another rank")
+
+    def _agree(self, ok: bool) -> bool:
+        """True on every rank if ``ok`` is true on every rank."""
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
+        return bool(flag.item())
+
+    def _self_test(self) -> str:
+        """One exchange step with exactly representable values: every rank sends rows and top-k rows tagged with its
+        rank and token, and returns partial rows whose bf16 sum over the ranks is exact.  Returns "" or what went
+        wrong."""
+        G, H, k, r, dev = self.world, self.H, self.k, self.rank, self.device
+        T = 2
+        try:
+            t = torch.arange(T, device=dev, dtype=torch.float32)[:, None]
+            x = (r + 0.25 * t).expand(T, H).to(torch.bfloat16).contiguous()
+            s = torch.arange(k, device=dev, dtype=torch.int32)[None, :]
+            ids = (r * 100 + 10 * t.to(torch.int32) + s).contiguous()
+            wts = (r + s.to(torch.float32) / 8).expand(T, k).contiguous()
+            self.dispatch(x, ids, wts)
+            xr, ids_r, w_r = self.recv(T)
+            d = torch.arange(G, device=dev, dtype=torch.float32).repeat_interleave(T)[:, None]
+            tt = torch.arange(T, device=dev, dtype=torch.float32).repeat(G)[:, None]
+            want_x = (d + 0.25 * tt).expand(G * T, H).to(torch.bfloat16)
+            want_ids = (d.to(torch.int32) * 100 + 10 * tt.to(torch.int32) + s)
+            want_w = (d + s.to(torch.float32) / 8)
+            # the partial row every rank returns for rank d's token t is (d + 1) + 2 t, so rank r's combined row t
+            # is G (r + 1 + 2 t): exact in bf16 for up to 32 ranks, and wrong if a row reached the wrong rank
+            parts = ((d + 1) + 2 * tt).expand(G * T, H).to(torch.bfloat16).contiguous()
+            out = self.combine(parts, T)
+            want_out = (G * (r + 1 + 2 * t)).expand(T, H).to(torch.bfloat16)
+            torch.cuda.synchronize(dev)
+            st = self.device_status()
+            if st:
+                return f"rank {r}: device status {st}"
+            if not (torch.equal(xr, want_x) and torch.equal(ids_r, want_ids) and torch.equal(w_r, want_w)):
+                return f"rank {r}: received rows differ from what the peers sent"
+            if not torch.equal(out, want_out):
+                return f"rank {r}: combined partial sums differ"
+            return ""
+        except Exception as e:  # noqa: BLE001 - reported to every rank
+            return f"rank {r}: {e}"
 
     def recv(self, T: int):
         """This step's received rows: x bf16 [G T, H], ids int32 [G T, k], weights fp32 [G T, k] (views/copies)."""
@@ -226,10 +284,14 @@ class ExpertParallelMoE:
         self.last = {}
         # dense steps over NVLink peer memory (GPU ranks only; collective construction)
         self.p2p = None
+        self.p2p_error = None
         if p2p and isinstance(_ops, CudaEpOps) and self.world > 1:
             H = w13.shape[2] * 2
-            self.p2p = P2PExchange(_ops.lib, group, self.rank, self.world, self.DENSE_MAX_TOKENS, H, top_k,
-                                   _ops.device)
+            try:
+                self.p2p = P2PExchange(_ops.lib, group, self.rank, self.world, self.DENSE_MAX_TOKENS, H, top_k,
+                                       _ops.device)
+            except P2PUnavailable as e:  # every rank lands here together: the dense step falls back to NCCL
+                self.p2p_error = str(e)
 
     def close(self):
         """Release the peer exchange (collective; before the process group is destroyed)."""
