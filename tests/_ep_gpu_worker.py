@@ -38,6 +38,8 @@ def nccl_worker(rank, world, port, E, H, I, T, k, seed, result_dir, p2p=True, ca
                 np.stack([torch.cat(got).view(torch.int16).cpu().numpy().view(np.uint16),
                           torch.cat(want).view(torch.int16).cpu().numpy().view(np.uint16)]))
         np.save(os.path.join(result_dir, f"nccl_status_{rank}.npy"), np.array([st]))
+        with open(os.path.join(result_dir, f"p2p_{rank}.txt"), "w") as f:  # whether the peer exchange was used
+            f.write("" if (not p2p or ep.p2p is not None) else (ep.p2p_error or "not set up"))
     finally:
         if ep is not None:
             ep.close()

@@ -30,6 +30,9 @@ def test_ep_two_gpus_match_single_gpu(tmp_path, T, p2p, calls):
     mp.spawn(nccl_worker, args=(world, _free_port(), E, H, I, T, k, 77, str(tmp_path), p2p, calls), nprocs=world,
              join=True)
     for r in range(world):
+        with open(os.path.join(tmp_path, f"p2p_{r}.txt")) as f:
+            why = f.read()
+        assert not why, f"rank {r}: the peer exchange was requested but not set up: {why}"
         assert int(np.load(os.path.join(tmp_path, f"nccl_status_{r}.npy"))[0]) == 0
         got, want = np.load(os.path.join(tmp_path, f"nccl_{r}.npy"))
         assert_close_bf16(torch.from_numpy(got.view(np.int16)).view(torch.bfloat16), want)
