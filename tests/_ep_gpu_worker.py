@@ -44,3 +44,37 @@ def nccl_worker(rank, world, port, E, H, I, T, k, seed, result_dir, p2p=True, ca
         if ep is not None:
             ep.close()
         dist.destroy_process_group()
+
+
+def p2p_single_rank_worker(rank, port, result_dir):
+    """One rank: the peer exchange's set-up (mapping agreement and self-test), two exchange steps and close."""
+    from xcalibur_b200 import _lib
+    from xcalibur_b200.ep import P2PExchange
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60))
+    msg = ""
+    try:
+        ex = P2PExchange(_lib.load(), None, 0, 1, 32, 1024, 8, dev)
+        for T in (1, 5):
+            x = torch.randn((T, 1024), device=dev).to(torch.bfloat16)
+            ids = torch.randint(0, 64, (T, 8), device=dev, dtype=torch.int32)
+            wts = torch.rand((T, 8), device=dev)
+            ex.dispatch(x, ids, wts)
+            xr, ids_r, w_r = ex.recv(T)
+            out = ex.combine(xr.clone(), T)
+            torch.cuda.synchronize()
+            if not (torch.equal(xr, x) and torch.equal(ids_r, ids) and torch.equal(w_r, wts) and torch.equal(out, x)):
+                msg += f"T={T}: round trip differs; "
+        if ex.device_status():
+            msg += "device status set; "
+        ex.close()
+    except Exception as e:  # noqa: BLE001 - reported to the test
+        msg += repr(e)
+    finally:
+        dist.destroy_process_group()
+    with open(os.path.join(result_dir, "p2p_single.txt"), "w") as f:
+        f.write(msg)

@@ -82,3 +82,14 @@ def test_p2p_exchange_one_rank_round_trip(cuda_device):
     finally:
         torch.cuda.synchronize(cuda_device)
         lib.xcb_p2p_free(own)
+
+
+def test_p2p_exchange_set_up_on_one_rank(tmp_path, cuda_device):
+    """The exchange object on a one-rank process group: its set-up (mapping agreement and exact-value self-test)
+    passes, two steps round-trip, and close releases it (in a child process, so no process group is left here)."""
+    from tests._ep_gpu_worker import p2p_single_rank_worker
+
+    mp.spawn(p2p_single_rank_worker, args=(_free_port(), str(tmp_path)), nprocs=1, join=True)
+    with open(os.path.join(tmp_path, "p2p_single.txt")) as f:
+        msg = f.read()
+    assert msg == "", msg
