@@ -4,8 +4,9 @@
  * entry point, okc_run(w, scratch, x, topk_ids, topk_weights, out, lo, nloc, grid) (moe_w4a16.py:2812, declared
  * at :3063-3068), builds its packed weights in Python in prepare() (moe_w4a16.py:3292-3351) and allocates its
  * scratch in _make_scratch() (moe_w4a16.py:3353-3367).  Here every argument is a plain device pointer plus sizes,
- * every call takes an explicit cudaStream_t, and the library never allocates: the caller provides the packed
- * weight buffers and the workspace, sized by the *_bytes queries.
+ * every call takes an explicit cudaStream_t, and the compute calls never allocate: the caller provides the packed
+ * weight buffers and the workspace, sized by the *_bytes queries (the expert-parallel set-up call xcb_p2p_alloc
+ * is the one call that allocates, once, the peer-exchange buffer).
  *
  * All calls return XCB_OK or an XCB_ERR_* code; argument and shape errors are detected on the host before any
  * launch.  Errors that only the device can see (a NaN block scale, an expert id out of range, a spin-wait that
