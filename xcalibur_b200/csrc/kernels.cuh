@@ -95,6 +95,7 @@ struct WideParams {
   float* y;                // mode 1 output, fp32 [routes, H]
   float* ss;               // mode 1 post-norm sums of squares [routes]
   int* status;
+  int* tilectl;            // [2] tiles claimed so far, CTAs finished (zero between launches)
   int E_loc, R, K, I, H;
   int mode, post_norm;
   unsigned long long timeout_ns;

@@ -11,7 +11,8 @@
 //   wide(1)  y[q] = down_e inter[q] * gs (* (1 + post_norm_w)), ss[q] += sum y^2 in post-norm mode   (fp32)
 //   combine  out[t] = bf16(sum_s w_s (* rsqrt(ss/H + 1e-8)) y[pos[t, s]])          (slot order, as the reference)
 //
-// wide_kernel is persistent (one CTA per SM, 640 threads, static round-robin over tiles).  A tile is 128 packed
+// wide_kernel is persistent (one CTA per SM, 640 threads; the weight-stream warp claims tiles in order from one
+// counter shared by all CTAs and hands them to the other roles through a shared-memory ring).  A tile is 128 packed
 // weight rows of one expert x up to 192 of its tokens, the full reduction length:
 //
 //   warp 0       streams the tile's packed weights (18 KB bulk copies, the prefill layout) into a 4-stage ring;
@@ -59,7 +60,9 @@ constexpr int kWdEpiWarp0 = 4 + 4 * kWdDq;
 constexpr int kWdEpiWarps = 8;     // two per tensor-memory lane quarter, one per 128-column half
 constexpr int kWdThreads = 32 * (kWdEpiWarp0 + kWdEpiWarps);
 constexpr int kWdXbuf = 4 * 2 * 32 * 17;  // SwiGLU exchange: [pair][gate|up][32 lanes][16 tokens + 1]
-constexpr int kWdNBar = 2 * kWdWSt + 2 * kWdASlots + 4 + 1;
+constexpr int kWdTQ = 8;  // tile ring: tiles claimed by the weight-stream warp, read in order by every other role
+constexpr int kWdTQReaders = 2 + 4 * kWdDq + kWdEpiWarps;  // activation producer, MMA, dequantising, epilogue warps
+constexpr int kWdNBar = 2 * kWdWSt + 2 * kWdASlots + 4 + 1 + 2 * kWdTQ;
 constexpr size_t kWdOffB = (size_t)kWdWSt * kWdStage;  // 1024-aligned (swizzle atoms)
 constexpr size_t kWdOffX = kWdOffB + (size_t)kWdBSt * kWdBBytes;
 constexpr size_t kWdOffBar = kWdOffX + (size_t)kWdXbuf * 4;
@@ -134,6 +137,27 @@ __device__ __forceinline__ bool wd_wait(uint64_t* bar, uint32_t par, volatile in
   return true;
 }
 
+// Tile n of this CTA's sequence, as published by the weight-stream warp (-1: no more tiles, or an abort).  The
+// whole warp calls wd_next_tile_warp (every lane gets lane 0's read, taken before lane 0 releases the slot); a
+// single thread calls wd_next_tile_one.
+__device__ __forceinline__ int wd_next_tile_warp(uint64_t* full, uint64_t* empty, volatile int* tq, uint32_t n,
+                                                 volatile int* abrt, const WideParams& p) {
+  const uint32_t s = n % kWdTQ;
+  const bool ok = __all_sync(0xffffffffu, wd_wait(full + s, (n / kWdTQ) & 1, abrt, p));
+  int i = ok ? tq[s] : -1;
+  i = __shfl_sync(0xffffffffu, i, 0);
+  if ((threadIdx.x & 31) == 0 && ok) mbar_arrive(empty + s);
+  return i;
+}
+__device__ __forceinline__ int wd_next_tile_one(uint64_t* full, uint64_t* empty, volatile int* tq, uint32_t n,
+                                                volatile int* abrt, const WideParams& p) {
+  const uint32_t s = n % kWdTQ;
+  if (!wd_wait(full + s, (n / kWdTQ) & 1, abrt, p)) return -1;
+  const int i = tq[s];
+  mbar_arrive(empty + s);
+  return i;
+}
+
 __device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
   __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
   return *reinterpret_cast<uint32_t*>(&r);
@@ -174,6 +198,9 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
   uint64_t* d_full = ab_empty + kWdASlots;  // [2]: accumulator b holds a finished tile
   uint64_t* d_empty = d_full + 2;           // [2]: the epilogue drained accumulator b
   uint64_t* drain = d_empty + 2;
+  uint64_t* tq_full = drain + 1;           // [kWdTQ]: tile slot published
+  uint64_t* tq_empty = tq_full + kWdTQ;    // [kWdTQ]: every reader has taken it
+  volatile int* tq = reinterpret_cast<volatile int*>(sm + kWdOffMisc + 32);
   int* offs = reinterpret_cast<int*>(sm + kWdOffTab);
   int* tpre = offs + 516;
   volatile int* abrt = reinterpret_cast<volatile int*>(sm + kWdOffMisc);
@@ -196,6 +223,10 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
       mbar_init(d_empty + b, kWdEpiWarps);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < kWdTQ; ++i) {
+      mbar_init(tq_full + i, 1);
+      mbar_init(tq_empty + i, kWdTQReaders);
+    }
     *abrt = 0;
     fence_mbar_init();
   }
@@ -220,9 +251,28 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
   if (warp == 0) {
     // ---------------------------------------------------------------- weight stream
     if (lane == 0) {
-      uint32_t ws = 0;
+      uint32_t ws = 0, nq = 0;
       bool ok = true;
-      for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x) {
+      // tiles are claimed in order from one counter shared by all CTAs (a CTA on a slower SM, or with narrower
+      // tiles, simply claims fewer), and published to this CTA's other roles through the tile ring
+      auto publish = [&](int i) -> bool {
+        const uint32_t s = nq % kWdTQ;
+        if (nq >= (uint32_t)kWdTQ && !wd_wait(tq_empty + s, ((nq / kWdTQ) + 1) & 1, abrt, p)) return false;
+        tq[s] = i;
+        mbar_arrive(tq_full + s);
+        ++nq;
+        return true;
+      };
+      for (;;) {
+        const int i = atomicAdd(p.tilectl, 1);
+        if (i >= ntiles) {
+          publish(-1);
+          break;
+        }
+        if (!publish(i)) {
+          ok = false;
+          break;
+        }
         const WdTile t = wd_tile(i, tpre, offs, E, RB);
         const uint8_t* src = p.w + ((size_t)t.e * RB + t.rb) * (size_t)nS * kWdStage;
         for (int s = 0; s < nS; ++s) {
@@ -237,6 +287,7 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
           bulk_g2s(wring + (size_t)slot * kWdStage, src + (size_t)s * kWdStage, kWdStage, w_full + slot);
           ++ws;
         }
+        if (!ok) break;
       }
       for (uint32_t u = ws > (uint32_t)kWdWSt ? ws - kWdWSt : 0; u < ws; ++u)  // copies still landing
         mbar_wait(w_full + (u & (kWdWSt - 1)), (u / kWdWSt) & 1, p.timeout_ns, p.status);
@@ -246,7 +297,9 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
     if (lane == 0) {
       uint32_t bs = 0;
       bool ok = true;
-      for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x) {
+      for (uint32_t n = 0; ok; ++n) {
+        const int i = wd_next_tile_one(tq_full, tq_empty, tq, n, abrt, p);
+        if (i < 0) break;
         const WdTile t = wd_tile(i, tpre, offs, E, RB);
         const CUtensorMap* tm = t.n <= 64 ? &maps.m64 : (t.n <= 128 ? &maps.m128 : &maps.m256);
         const uint32_t bytes = (t.n <= 64 ? 64u : (t.n <= 128 ? 128u : 256u)) * 128u;
@@ -278,7 +331,9 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
     const uint64_t bdesc0 = sdesc_sw128(smem_u32(bring));
     bool ok = true;
     WD_PROF_T0(t_all);
-    for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x, ++tc) {
+    for (uint32_t n = 0; ok; ++n, ++tc) {
+      const int i = wd_next_tile_warp(tq_full, tq_empty, tq, n, abrt, p);
+      if (i < 0) break;
       const WdTile t = wd_tile(i, tpre, offs, E, RB);
       const uint32_t idesc = idesc_bf16_m128(max(16, (t.n + 15) & ~15));
       WD_PROF_T0(t_d);
@@ -329,7 +384,8 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
     uint32_t gc = 0;
     bool ok = true;
     WD_PROF_T0(t_all);
-    for (int i = blockIdx.x; i < ntiles && ok; i += gridDim.x) {
+    for (uint32_t n = 0; ok; ++n) {
+      if (wd_next_tile_warp(tq_full, tq_empty, tq, n, abrt, p) < 0) break;
       for (int c = 0; c < nK; ++c, ++gc) {
         if ((int)(gc % kWdDq) != grp) continue;
         const uint32_t st = gc >> 2, wslot = st & (kWdWSt - 1), aslot = gc & (kWdASlots - 1);
@@ -368,7 +424,9 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
     const uint32_t tlane = (uint32_t)(32 * wq) << 16;
     uint32_t tc = 0;
     WD_PROF_T0(t_all);
-    for (int i = blockIdx.x; i < ntiles; i += gridDim.x, ++tc) {
+    for (uint32_t n = 0;; ++n, ++tc) {
+      const int i = wd_next_tile_warp(tq_full, tq_empty, tq, n, abrt, p);
+      if (i < 0) break;
       const WdTile t = wd_tile(i, tpre, offs, E, RB);
       const float gsc = p.gs[t.e] * kTwo52;  // loaded while the MMAs run
       WD_PROF_T0(t_d);
@@ -445,6 +503,15 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+  // the last CTA to finish returns the tile counter and its own count to zero for the next launch
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(p.tilectl + 1, 1) == (int)gridDim.x - 1) {
+      p.tilectl[0] = 0;
+      p.tilectl[1] = 0;
+      __threadfence();
+    }
   }
 }
 
@@ -556,6 +623,7 @@ int launch_wide_path(const WidePathParams& a, cudaStream_t stream) {
   g.I = a.I;
   g.H = a.H;
   g.status = a.ctl + kCtlStatus;
+  g.tilectl = a.ctl + kCtlWideTile;
   g.timeout_ns = a.timeout_ns;
   g.normw = a.normw;
   g.post_norm = a.post_norm;

@@ -19,6 +19,7 @@ enum CtlWord : int {
   kCtlExit = 2,        // CTAs that finished the decode-path kernel (the last one resets the counters)
   kCtlJobs = 3,        // number of jobs written by the router
   kCtlRoutes = 4,      // number of local routes
+  kCtlWideTile = 5,    // [2] prefill GEMM tile claims and finished CTAs (the last CTA resets both)
   kCtlDoneA = 64,      // [256] per-job phase-A counters when the decode kernel routes in-kernel
   kCtlSS = 320,        // [256] fp32 per-route sums of squares (post-norm) when routing in-kernel
   kCtlRowBlock = 576,  // [512] per-16-row-block phase-B arrival counters (H <= 8192)
