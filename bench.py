@@ -10,8 +10,11 @@ each GPU holds E / N experts and its own tokens, which travel to the experts' GP
   Weights are 6.3 GB resident (>> 126 MB L2) and every step uses a different input from a pool of 64, so each
   step streams experts that the previous steps did not touch.
 * ``e2e``: the same metric through the public API with pinned HOST inputs: every step copies x and the router
-  logits host->device, runs the layer and copies the output device->host.
-* ``roofline``: the experts kernel (``skinny_kernel``), timed alone with events around its launch:
+  logits host->device, runs the layer and copies the output device->host; on one GPU the copies run on a second
+  stream against two device buffer sets (a serving loop's double buffering), on several GPUs in line with the
+  captured step.
+* ``roofline``: the experts kernel (``skinny_kernel``), timed with events (over the K back-to-back launches when a
+  step is one launch; ``kernel_ms_bracketed`` brackets every launch):
   algorithmic bytes = distinct experts touched x (FP4 codes + E4M3 scales + global scales) + x + out.
 * ``cpu_baseline``: the CPU oracle (a torch/numpy fp32 restatement of the layer; the reference has no CPU
   implementation) on the host cores, on a bounded sample (one token for decode).
