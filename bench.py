@@ -407,11 +407,12 @@ def run_xcb_ep(a, cfg, rank, world, dist):
                            f"routes per rank per step")
     # per step: top-k, plan, gather, combine + the local layer (one decode launch, or router + gather + two grouped
     # GEMMs + combine on the prefill path)
-    # this library's kernels per step: router top-k, then the exchange (peer dispatch + combine; or NCCL with the
-    # combine kernel; or plan + gather + combine), and the local layer (one launch up to 256 local routes, else 5)
+    # this library's kernels per step: the exchange (peer dispatch with the router inside + peer combine; or router
+    # top-k + NCCL + combine kernel; or router + plan + gather + combine) and the local layer (one launch up to 256
+    # local routes, else 5)
     local = 1 if world * T * k <= 256 else 5
     if T <= ExpertParallelMoE.DENSE_MAX_TOKENS:
-        res["gpu_launches"] = K * ((3 if dense_p2p else 2) + local)
+        res["gpu_launches"] = K * (2 + local)
     else:
         res["gpu_launches"] = K * (4 + local)
     return res

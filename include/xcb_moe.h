@@ -201,9 +201,11 @@ int xcb_ep_combine(const uint16_t* parts, const int32_t* counts, const int32_t* 
  * xcb_p2p_alloc (zeroed; handle = 64-byte CUDA IPC handle to share with the other ranks), opens the others'
  * with xcb_p2p_open, and passes peers = device uint64 [G] (peers[d] = rank d's buffer in this process, peers[rank]
  * its own).  Layout of a buffer for a step of T tokens: x bf16 [G * T, H] (row d*T + t = token t of rank d),
- * meta int32 [G * T, 2k] (k ids, then k fp32 weight bit patterns), partial sums bf16 [G * T, H], flags.
- * xcb_ep_p2p_dispatch writes this rank's rows into every buffer and returns once (in stream order) every rank's
- * rows are in this rank's buffer; the local layer then runs on them; xcb_ep_p2p_combine sends partial rows
+ * top-k ids int32 [G * T, k], top-k weights fp32 [G * T, k], partial sums bf16 [G * T, H], flags.
+ * xcb_ep_p2p_dispatch routes this rank's tokens (router logits fp32 [T, E], E <= 512: the same softmax -> top-k
+ * -> renormalise as xcb_moe_topk), writes their rows and top-k rows into every buffer and returns once (in stream
+ * order) every rank's rows are in this rank's buffer; the local layer then runs on them in place;
+ * xcb_ep_p2p_combine sends partial rows
  * [d*T, (d+1)*T) to rank d and writes out bf16 [T, H] = sum over source ranks in rank order.  Every rank must make
  * the same calls in the same order.  Waits are bounded (2 s): status gets XCB_STATUS_DEVICE_TIMEOUT. */
 size_t xcb_ep_p2p_bytes(int32_t G, int32_t T_max, int32_t H, int32_t k);
@@ -211,7 +213,7 @@ int xcb_p2p_alloc(size_t bytes, void** ptr, void* handle);
 int xcb_p2p_open(const void* handle, void** ptr);
 int xcb_p2p_close(void* ptr);
 int xcb_p2p_free(void* ptr);
-int xcb_ep_p2p_dispatch(const uint16_t* x, const int32_t* ids, const float* wts, int32_t T, int32_t T_max, int32_t H,
+int xcb_ep_p2p_dispatch(const uint16_t* x, const float* logits, int32_t T, int32_t T_max, int32_t H, int32_t E,
                         int32_t k, int32_t G, int32_t rank, const uint64_t* peers, int32_t* status,
                         cudaStream_t stream);
 int xcb_ep_p2p_combine(const uint16_t* parts, int32_t T, int32_t T_max, int32_t H, int32_t k, int32_t G,

@@ -58,12 +58,16 @@ def p2p_single_rank_worker(rank, port, result_dir):
     dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60))
     msg = ""
     try:
-        ex = P2PExchange(_lib.load(), None, 0, 1, 32, 1024, 8, dev)
+        lib = _lib.load()
+        ex = P2PExchange(lib, None, 0, 1, 32, 1024, 64, 8, dev)
+        stream = torch.cuda.current_stream(dev).cuda_stream
         for T in (1, 5):
             x = torch.randn((T, 1024), device=dev).to(torch.bfloat16)
-            ids = torch.randint(0, 64, (T, 8), device=dev, dtype=torch.int32)
-            wts = torch.rand((T, 8), device=dev)
-            ex.dispatch(x, ids, wts)
+            logits = torch.randn((T, 64), device=dev)
+            ids = torch.empty((T, 8), dtype=torch.int32, device=dev)
+            wts = torch.empty((T, 8), dtype=torch.float32, device=dev)
+            lib.xcb_moe_topk(logits.data_ptr(), T, 64, 8, ids.data_ptr(), wts.data_ptr(), stream)
+            ex.dispatch(x, logits)
             xr, ids_r, w_r = ex.recv(T)
             out = ex.combine(xr.clone(), T)
             torch.cuda.synchronize()

@@ -40,44 +40,48 @@ def test_ep_two_gpus_match_single_gpu(tmp_path, T, p2p, calls):
 
 def test_p2p_exchange_one_rank_round_trip(cuda_device):
     """The peer-exchange kernels on one rank (its buffer is its only peer; one block per peer, so each kernel
-    raises the flag it then waits for): the received rows and top-k rows equal what was sent, the combine returns
-    the partial rows summed over the one rank, and three consecutive steps keep the per-step flags in step."""
+    raises the flag it then waits for): the received rows equal what was sent, the received top-k rows equal the
+    library router's on the same logits, the combine returns the partial rows summed over the one rank, and three
+    consecutive steps keep the per-step flags in step."""
     import ctypes
 
     from xcalibur_b200 import _lib
     from xcalibur_b200.ep import _DeviceBytes, p2p_layout
 
     lib = _lib.load()
-    G, Tm, H, k = 1, 4, 256, 4
+    G, Tm, H, E, k = 1, 4, 256, 64, 4
     nbytes = lib.xcb_ep_p2p_bytes(G, Tm, H, k)
     own = ctypes.c_void_p()
     handle = (ctypes.c_ubyte * 64)()
     assert lib.xcb_p2p_alloc(nbytes, ctypes.byref(own), handle) == _lib.XCB_OK
     try:
         buf = torch.as_tensor(_DeviceBytes(own.value, nbytes), device=cuda_device)
-        xo, mo, _, _, _ = p2p_layout(G, Tm, H, k)
+        xo, io, wo, _, _, _ = p2p_layout(G, Tm, H, k)
         peers = torch.tensor([own.value], dtype=torch.int64, device=cuda_device)
         status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
         stream = torch.cuda.current_stream(cuda_device).cuda_stream
         g = torch.Generator(device=cuda_device).manual_seed(5)
         for step, T in enumerate((3, 1, 4)):
             x = torch.randn((T, H), generator=g, device=cuda_device).to(torch.bfloat16)
-            ids = torch.randint(0, 64, (T, k), generator=g, device=cuda_device, dtype=torch.int32)
-            wts = torch.rand((T, k), generator=g, device=cuda_device)
-            assert lib.xcb_ep_p2p_dispatch(x.data_ptr(), ids.data_ptr(), wts.data_ptr(), T, Tm, H, k, G, 0,
-                                           peers.data_ptr(), status.data_ptr(), stream) == _lib.XCB_OK
+            logits = torch.randn((T, E), generator=g, device=cuda_device)
+            ids = torch.empty((T, k), dtype=torch.int32, device=cuda_device)
+            wts = torch.empty((T, k), dtype=torch.float32, device=cuda_device)
+            assert lib.xcb_moe_topk(logits.data_ptr(), T, E, k, ids.data_ptr(), wts.data_ptr(), stream) == _lib.XCB_OK
+            assert lib.xcb_ep_p2p_dispatch(x.data_ptr(), logits.data_ptr(), T, Tm, H, E, k, G, 0, peers.data_ptr(),
+                                           status.data_ptr(), stream) == _lib.XCB_OK
             parts = torch.randn((T, H), generator=g, device=cuda_device).to(torch.bfloat16)
             out = torch.empty((T, H), dtype=torch.bfloat16, device=cuda_device)
             torch.cuda.synchronize(cuda_device)
             xr = buf[xo:xo + T * H * 2].view(torch.bfloat16).view(T, H).clone()
-            meta = buf[mo:mo + T * 2 * k * 4].view(torch.int32).view(T, 2 * k).clone()
+            ids_r = buf[io:io + T * k * 4].view(torch.int32).view(T, k).clone()
+            w_r = buf[wo:wo + T * k * 4].view(torch.float32).view(T, k).clone()
             assert lib.xcb_ep_p2p_combine(parts.data_ptr(), T, Tm, H, k, G, 0, peers.data_ptr(), out.data_ptr(),
                                           status.data_ptr(), stream) == _lib.XCB_OK
             torch.cuda.synchronize(cuda_device)
             assert int(status.item()) == 0, f"step {step}: device status {int(status.item())}"
             assert torch.equal(xr, x)
-            assert torch.equal(meta[:, :k], ids)
-            assert torch.equal(meta[:, k:].view(torch.float32), wts)
+            assert torch.equal(ids_r, ids)
+            assert torch.equal(w_r, wts)
             assert torch.equal(out, parts)
     finally:
         torch.cuda.synchronize(cuda_device)

@@ -114,7 +114,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "xcb_p2p_open": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_void_p)]),
         "xcb_p2p_close": (ctypes.c_int, [P]),
         "xcb_p2p_free": (ctypes.c_int, [P]),
-        "xcb_ep_p2p_dispatch": (ctypes.c_int, [P, P, P, I32, I32, I32, I32, I32, I32, P, P, P]),
+        "xcb_ep_p2p_dispatch": (ctypes.c_int, [P, P, I32, I32, I32, I32, I32, I32, I32, P, P, P]),
         "xcb_ep_p2p_combine": (ctypes.c_int, [P, I32, I32, I32, I32, I32, I32, P, P, P, P]),
         "xcb_ep_gather": (ctypes.c_int, [P, P, P, I32, I32, I32, I32, P, P, P, P, P, P]),
         "xcb_ep_combine": (ctypes.c_int, [P, P, P, I32, I32, I32, P, P]),

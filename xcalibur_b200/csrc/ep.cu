@@ -230,14 +230,15 @@ int xcb_ep_combine(const uint16_t* parts, const int32_t* counts, const int32_t* 
 namespace xcb {
 
 struct P2pLayout {
-  size_t x, meta, part, flag, total;
+  size_t x, ids, wts, part, flag, total;
 };
 __host__ __device__ inline P2pLayout p2p_layout(int G, int Tm, int H, int k) {
   P2pLayout L;
   size_t o = 0;
   auto take = [&](size_t b) { size_t at = o; o = (o + b + 255) / 256 * 256; return at; };
   L.x = take((size_t)G * Tm * H * 2);
-  L.meta = take((size_t)G * Tm * 2 * k * 4);
+  L.ids = take((size_t)G * Tm * k * 4);
+  L.wts = take((size_t)G * Tm * k * 4);
   L.part = take((size_t)G * Tm * H * 2);
   L.flag = take((size_t)(2 * G + 4) * 4);  // x flags [G], part flags [G], epoch, block counter
   L.total = o;
@@ -270,10 +271,9 @@ __device__ bool p2p_wait_all(const unsigned* flags, int G, unsigned target, uint
   return true;
 }
 
-__global__ void ep_p2p_dispatch_kernel(const uint16_t* __restrict__ x, const int* __restrict__ ids,
-                                       const float* __restrict__ wts, int T, int Tm, int H, int k, int G, int rank,
-                                       const uint64_t* __restrict__ peers, int nb, P2pLayout L, uint64_t timeout_ns,
-                                       int* status) {
+__global__ void ep_p2p_dispatch_kernel(const uint16_t* __restrict__ x, const float* __restrict__ logits, int T, int Tm,
+                                       int H, int E, int k, int G, int rank, const uint64_t* __restrict__ peers,
+                                       int nb, P2pLayout L, uint64_t timeout_ns, int* status) {
   (void)Tm;
   const int d = blockIdx.x / nb, sub = blockIdx.x % nb;
   uint8_t* mine = reinterpret_cast<uint8_t*>(peers[rank]);
@@ -285,11 +285,19 @@ __global__ void ep_p2p_dispatch_kernel(const uint16_t* __restrict__ x, const int
   // slots are T rows apart (every rank sends T rows this step), so the received rows form one [G T, H] matrix
   uint4* dx = reinterpret_cast<uint4*>(dst + L.x + (size_t)rank * T * H * 2);
   for (int i = r0 * nv + threadIdx.x; i < r1 * nv; i += blockDim.x) dx[i] = __ldg(src + i);
-  int* dm = reinterpret_cast<int*>(dst + L.meta + (size_t)rank * T * 2 * k * 4);
-  for (int i = r0 * k + threadIdx.x; i < r1 * k; i += blockDim.x) {
-    const int t = i / k, s = i % k;
-    dm[t * 2 * k + s] = ids[i];
-    dm[t * 2 * k + k + s] = __float_as_int(wts[i]);
+  // the router: top-k of each of this block's tokens (one warp per token; every block sending these rows computes
+  // the same selection), written straight into the peer's ids / weights slots
+  int* di = reinterpret_cast<int*>(dst + L.ids + (size_t)rank * T * k * 4);
+  float* dw = reinterpret_cast<float*>(dst + L.wts + (size_t)rank * T * k * 4);
+  const int lane = threadIdx.x & 31;
+  for (int t = r0 + (threadIdx.x >> 5); t < r1; t += blockDim.x >> 5) {
+    int id;
+    float w;
+    warp_topk(logits + (size_t)t * E, E, k, id, w);
+    if (lane < k) {
+      di[t * k + lane] = id;
+      dw[t * k + lane] = w;
+    }
   }
   __threadfence_system();
   __syncthreads();
@@ -403,15 +411,15 @@ static int p2p_blocks(int T, int H) {
   return (int)(nb > T ? T : nb);
 }
 
-int xcb_ep_p2p_dispatch(const uint16_t* x, const int32_t* ids, const float* wts, int32_t T, int32_t T_max, int32_t H,
+int xcb_ep_p2p_dispatch(const uint16_t* x, const float* logits, int32_t T, int32_t T_max, int32_t H, int32_t E,
                         int32_t k, int32_t G, int32_t rank, const uint64_t* peers, int32_t* status,
                         cudaStream_t stream) {
-  if (T <= 0 || T > T_max || H <= 0 || H % 8 || k <= 0 || k > 16 || G <= 0 || G > kEpMaxRanks || rank < 0 ||
-      rank >= G)
+  if (T <= 0 || T > T_max || H <= 0 || H % 8 || E <= 0 || E > 512 || k <= 0 || k > 16 || k > E || G <= 0 ||
+      G > kEpMaxRanks || rank < 0 || rank >= G)
     return XCB_ERR_INVALID_ARG;
-  if (!x || !ids || !wts || !peers || !status || ((uintptr_t)x & 15u)) return XCB_ERR_INVALID_ARG;
+  if (!x || !logits || !peers || !status || ((uintptr_t)x & 15u)) return XCB_ERR_INVALID_ARG;
   const int nb = p2p_blocks(T, H);
-  ep_p2p_dispatch_kernel<<<G * nb, 256, 0, stream>>>(x, ids, wts, T, T_max, H, k, G, rank, peers, nb,
+  ep_p2p_dispatch_kernel<<<G * nb, 256, 0, stream>>>(x, logits, T, T_max, H, E, k, G, rank, peers, nb,
                                                      p2p_layout(G, T_max, H, k), 2000000000ull, status);
   return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
 }

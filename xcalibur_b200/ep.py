@@ -39,7 +39,7 @@ def _stream(device: torch.device) -> int:
 
 
 def p2p_layout(G: int, T_max: int, H: int, k: int):
-    """Byte offsets (x, meta, part, flag) and total size of a peer-exchange buffer (mirrors the C library's)."""
+    """Byte offsets (x, ids, wts, part, flag) and total size of a peer-exchange buffer (mirrors the C library's)."""
     o = 0
 
     def take(b):
@@ -49,10 +49,11 @@ def p2p_layout(G: int, T_max: int, H: int, k: int):
         return at
 
     x = take(G * T_max * H * 2)
-    meta = take(G * T_max * 2 * k * 4)
+    ids = take(G * T_max * k * 4)
+    wts = take(G * T_max * k * 4)
     part = take(G * T_max * H * 2)
     flag = take((2 * G + 4) * 4)
-    return x, meta, part, flag, o
+    return x, ids, wts, part, flag, o
 
 
 class _DeviceBytes:
@@ -74,12 +75,12 @@ class P2PExchange:
     and a one-step self-test are checked by all ranks together) and must ``close`` it before the process group is
     destroyed.  Raises ``P2PUnavailable`` on every rank if any rank failed, after releasing what it set up."""
 
-    def __init__(self, lib, group, rank: int, world: int, T_max: int, H: int, k: int, device):
+    def __init__(self, lib, group, rank: int, world: int, T_max: int, H: int, E: int, k: int, device):
         self.lib, self.group, self.rank, self.world = lib, group, rank, world
-        self.T_max, self.H, self.k, self.device = T_max, H, k, device
+        self.T_max, self.H, self.E, self.k, self.device = T_max, H, E, k, device
         self.offs = p2p_layout(world, T_max, H, k)
         nbytes = int(lib.xcb_ep_p2p_bytes(world, T_max, H, k))
-        if nbytes != self.offs[4]:
+        if nbytes != self.offs[5]:
             raise RuntimeError("peer-exchange layout mismatch between the library and its Python mirror")
         own = ctypes.c_void_p()
         handle = (ctypes.c_ubyte * 64)()
@@ -119,25 +120,32 @@ class P2PExchange:
         dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
         return bool(flag.item())
 
+    def _logits_of(self, d: int, T: int):
+        """Deterministic router logits of rank d for the self-test (identical on every rank)."""
+        g = torch.Generator(device=self.device).manual_seed(7919 + d)
+        return torch.randn((T, self.E), generator=g, device=self.device, dtype=torch.float32)
+
     def _self_test(self) -> str:
-        """One exchange step with exactly representable values: every rank sends rows and top-k rows tagged with its
-        rank and token, and returns partial rows whose bf16 sum over the ranks is exact.  Returns "" or what went
-        wrong."""
+        """One exchange step with known values: every rank sends rows tagged with its rank and token and the top-k
+        of logits every rank can rebuild (checked against the library's own router), and returns partial rows whose
+        bf16 sum over the ranks is exact.  Returns "" or what went wrong."""
         G, H, k, r, dev = self.world, self.H, self.k, self.rank, self.device
         T = 2
         try:
             t = torch.arange(T, device=dev, dtype=torch.float32)[:, None]
             x = (r + 0.25 * t).expand(T, H).to(torch.bfloat16).contiguous()
-            s = torch.arange(k, device=dev, dtype=torch.int32)[None, :]
-            ids = (r * 100 + 10 * t.to(torch.int32) + s).contiguous()
-            wts = (r + s.to(torch.float32) / 8).expand(T, k).contiguous()
-            self.dispatch(x, ids, wts)
+            self.dispatch(x, self._logits_of(r, T))
             xr, ids_r, w_r = self.recv(T)
             d = torch.arange(G, device=dev, dtype=torch.float32).repeat_interleave(T)[:, None]
             tt = torch.arange(T, device=dev, dtype=torch.float32).repeat(G)[:, None]
             want_x = (d + 0.25 * tt).expand(G * T, H).to(torch.bfloat16)
-            want_ids = (d.to(torch.int32) * 100 + 10 * tt.to(torch.int32) + s)
-            want_w = (d + s.to(torch.float32) / 8)
+            want_ids = torch.empty((G * T, k), dtype=torch.int32, device=dev)
+            want_w = torch.empty((G * T, k), dtype=torch.float32, device=dev)
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            for src in range(G):
+                lg = self._logits_of(src, T)
+                check(self.lib.xcb_moe_topk(lg.data_ptr(), T, self.E, k, want_ids[src * T:].data_ptr(),
+                                            want_w[src * T:].data_ptr(), stream), "xcb_moe_topk")
             # the partial row every rank returns for rank d's token t is (d + 1) + 2 t, so rank r's combined row t
             # is G (r + 1 + 2 t): exact in bf16 for up to 32 ranks, and wrong if a row reached the wrong rank
             parts = ((d + 1) + 2 * tt).expand(G * T, H).to(torch.bfloat16).contiguous()
@@ -156,19 +164,22 @@ class P2PExchange:
             return f"rank {r}: {e}"
 
     def recv(self, T: int):
-        """This step's received rows: x bf16 [G T, H], ids int32 [G T, k], weights fp32 [G T, k] (views/copies)."""
+        """This step's received rows, in place: x bf16 [G T, H], top-k ids int32 [G T, k], weights fp32 [G T, k]."""
         G, H, k = self.world, self.H, self.k
-        xo, mo = self.offs[0], self.offs[1]
+        xo, io, wo = self.offs[0], self.offs[1], self.offs[2]
         xr = self.buf[xo:xo + G * T * H * 2].view(torch.bfloat16).view(G * T, H)
-        meta = self.buf[mo:mo + G * T * 2 * k * 4].view(torch.int32).view(G * T, 2 * k)
-        return xr, meta[:, :k].contiguous(), meta[:, k:].contiguous().view(torch.float32)
+        ids = self.buf[io:io + G * T * k * 4].view(torch.int32).view(G * T, k)
+        wts = self.buf[wo:wo + G * T * k * 4].view(torch.float32).view(G * T, k)
+        return xr, ids, wts
 
-    def dispatch(self, x, ids, wts):
+    def dispatch(self, x, logits):
+        """Route this rank's tokens (router logits fp32 [T, E]) and send their rows and top-k rows to every rank."""
         T = x.shape[0]
+        logits = logits.to(torch.float32).contiguous()
         stream = torch.cuda.current_stream(self.device).cuda_stream
-        check(self.lib.xcb_ep_p2p_dispatch(x.data_ptr(), ids.data_ptr(), wts.data_ptr(), T, self.T_max, self.H,
-                                           self.k, self.world, self.rank, self.peers.data_ptr(),
-                                           self.status.data_ptr(), stream), "xcb_ep_p2p_dispatch")
+        check(self.lib.xcb_ep_p2p_dispatch(x.data_ptr(), logits.data_ptr(), T, self.T_max, self.H, self.E, self.k,
+                                           self.world, self.rank, self.peers.data_ptr(), self.status.data_ptr(),
+                                           stream), "xcb_ep_p2p_dispatch")
 
     def combine(self, parts, T: int):
         out = torch.empty((T, self.H), dtype=torch.bfloat16, device=self.device)
@@ -288,8 +299,8 @@ class ExpertParallelMoE:
         if p2p and isinstance(_ops, CudaEpOps) and self.world > 1:
             H = w13.shape[2] * 2
             try:
-                self.p2p = P2PExchange(_ops.lib, group, self.rank, self.world, self.DENSE_MAX_TOKENS, H, top_k,
-                                       _ops.device)
+                self.p2p = P2PExchange(_ops.lib, group, self.rank, self.world, self.DENSE_MAX_TOKENS, H, self.E,
+                                       top_k, _ops.device)
             except P2PUnavailable as e:  # every rank lands here together: the dense step falls back to NCCL
                 self.p2p_error = str(e)
 
@@ -310,14 +321,17 @@ class ExpertParallelMoE:
     # returns a zero partial for it.  Small batches (decode) are latency-bound, and this halves their collectives.
     DENSE_MAX_TOKENS = 32
 
-    def _dense_p2p(self, x, ids, wts, top_k):
+    def _dense_p2p(self, x, router_logits, top_k):
+        """Three kernels per step: route + send (peer dispatch), the local layer on the received rows in place,
+        return + sum (peer combine)."""
         T = x.shape[0]
         ex = self.p2p
-        ex.dispatch(x, ids, wts)
+        ex.dispatch(x, router_logits)
         xr, ids_r, w_r = ex.recv(T)
         parts = self.ops.local(xr, ids_r, w_r, self.post_norm)
         out = ex.combine(parts, T)
-        self.last.update({"ids": ids, "wts": wts, "send": [T] * self.world, "recv": [T] * self.world,
+        mine = slice(self.rank * T, (self.rank + 1) * T)
+        self.last.update({"ids": ids_r[mine], "wts": w_r[mine], "send": [T] * self.world, "recv": [T] * self.world,
                           "recv_ids": ids_r})
         return out
 
@@ -353,10 +367,10 @@ class ExpertParallelMoE:
         T, H = x.shape
         if tuple(router_logits.shape) != (T, self.E):
             raise ValueError(f"router_logits must be [T, {self.E}]")
+        if 0 < T <= self.DENSE_MAX_TOKENS and self.p2p is not None and top_k == self.p2p.k:
+            return self._dense_p2p(x, router_logits, top_k)
         ids, wts = self.ops.topk(router_logits, top_k)
         if 0 < T <= self.DENSE_MAX_TOKENS:
-            if self.p2p is not None and top_k == self.p2p.k:
-                return self._dense_p2p(x, ids, wts, top_k)
             return self._dense(x, ids, wts, top_k)
         counts, send_tok, send_pos = self.ops.plan(ids, self.epr, self.world)
         recv_counts = torch.empty_like(counts)
