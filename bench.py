@@ -141,8 +141,19 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------------------------- CPU baseline
-def cpu_oracle_sample(weights_dev, x, logits, k, tokens: int):
-    """Time the CPU oracle on the first `tokens` tokens; returns (seconds, tokens, cores)."""
+def sample_routes(logits, k, tokens: int):
+    """Top-k routes of the first `tokens` tokens (CPU oracle router) and the distinct experts they use."""
+    import numpy as np
+
+    from oracle import moe_ref
+
+    ids, wts = moe_ref.route_topk(logits[:tokens].float().cpu().numpy(), k)
+    return ids, wts, np.unique(ids)
+
+
+def cpu_oracle_sample(host, used, x, ids, wts, tokens: int):
+    """Time the CPU oracle on the first `tokens` tokens; `host` holds the reference-layout arrays of the experts
+    `used` (in that order).  Returns (seconds, tokens, cores)."""
     import numpy as np
     import torch
 
@@ -150,19 +161,53 @@ def cpu_oracle_sample(weights_dev, x, logits, k, tokens: int):
 
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    xs = x[:tokens]
-    lg = logits[:tokens].float().cpu().numpy()
-    ids, wts = moe_ref.route_topk(lg, k)
-    used = np.unique(ids)
-    sel = torch.as_tensor(used, device=weights_dev["w13"].device)
-    host = {n: weights_dev[n].index_select(0, sel).cpu().numpy() for n in weights_dev}
     remap = {int(e): i for i, e in enumerate(used)}
     cid = np.vectorize(remap.get)(ids).astype(np.int32)
-    xb = xs.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    xb = x[:tokens].contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
     t0 = time.perf_counter()
     moe_ref.moe_forward(xb, cid, wts, host["w13"], host["w13_sf"], host["w13_gs"], host["w2"], host["w2_sf"],
                         host["w2_gs"])
     return time.perf_counter() - t0, tokens, cores
+
+
+def host_experts(weights_dev, used):
+    """The reference-layout arrays of the experts `used`, copied to the host from the device weights."""
+    import torch
+
+    sel = torch.as_tensor(used, device=weights_dev["w13"].device)
+    return {n: weights_dev[n].index_select(0, sel).cpu().numpy() for n in weights_dev}
+
+
+def reference_arm_experts(cfg, used, seed: int, device, std: float = 0.02, chunk: int = 8):
+    """The experts `used` of the seeded synthetic layer, built without this repository's CUDA library: the same
+    fp32 draws as ``xcalibur_b200.synth.make_weights`` (one device generator, gate_up then down per chunk of
+    `chunk` experts), quantised on the host by the CPU oracle's NVFP4 quantiser (bit-exact with the library's)."""
+    import numpy as np
+    import torch
+
+    from oracle import nvfp4
+
+    E, H, I = cfg["E"], cfg["H"], cfg["I"]
+    want = set(int(e) for e in used)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    got = {}
+    for e0 in range(0, E, chunk):
+        n = min(chunk, E - e0)
+        for name, shape in (("w13", (n, 2 * I, H)), ("w2", (n, H, I))):
+            w = torch.randn(shape, generator=g, device=device, dtype=torch.float32) * std
+            for e in range(e0, e0 + n):
+                if e in want:
+                    c, sf, gs = nvfp4.quantize(w[e - e0:e - e0 + 1].cpu().numpy())
+                    got[(name, e)] = (c[0], sf[0], gs[0])
+            del w
+    order = [int(e) for e in used]
+    host = {}
+    for name in ("w13", "w2"):
+        host[name] = np.stack([got[(name, e)][0] for e in order])
+        host[name + "_sf"] = np.stack([got[(name, e)][1] for e in order])
+        host[name + "_gs"] = np.array([got[(name, e)][2] for e in order], dtype=np.float32)
+    return host
 
 
 # ----------------------------------------------------------------------------------------------- main arm
@@ -180,7 +225,9 @@ def run_xcb(a, cfg, rank, world, dist):
     cpu = None
     if rank == 0 and not a.no_cpu_baseline:
         x0, l0 = synth.make_inputs(T, H, E, seed=1, device=dev, bias_std=cfg["bias_std"], zipf_s=cfg["zipf"])
-        cpu = cpu_oracle_sample(weights, x0, l0, k, min(T, a.cpu_sample_tokens))
+        n0 = min(T, a.cpu_sample_tokens)
+        ids0, wts0, used0 = sample_routes(l0, k, n0)
+        cpu = cpu_oracle_sample(host_experts(weights, used0), used0, x0, ids0, wts0, n0)
     del weights                                       # only the packed copy stays resident
     torch.cuda.empty_cache()
     P = max(1, a.pool if T <= 64 else 2)
@@ -533,19 +580,22 @@ def finish(a, cfg, world, ms, kern_ms, e2e_ms, u_avg, P, clk, cpu):
 
 
 def run_reference(a, cfg):
-    """Reference arm: the CPU restatement of the layer (the reference has no CPU implementation), per step."""
+    """Reference arm: the CPU restatement of the layer (the reference has no CPU implementation), per step.  It
+    loads nothing of this repository's CUDA library: the sampled tokens' experts are drawn and quantised on the
+    host (``reference_arm_experts``)."""
     import torch
 
-    from xcalibur_b200 import synth  # noqa: F401  (only for the byte/flop helpers)
+    from xcalibur_b200 import synth  # noqa: F401  (torch-only input generator; the library is not loaded)
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     E, H, I, T, k = cfg["E"], cfg["H"], cfg["I"], cfg["T"], cfg["k"]
-    weights = synth.make_weights(E, H, I, seed=1234, device=dev)
-    x, lg = synth.make_inputs(T, H, E, seed=1, device=dev, bias_std=cfg["bias_std"])
+    x, lg = synth.make_inputs(T, H, E, seed=1, device=dev, bias_std=cfg["bias_std"], zipf_s=cfg["zipf"])
     n = min(T, a.cpu_sample_tokens)
+    ids, wts, used = sample_routes(lg, k, n)
+    host = reference_arm_experts(cfg, used, seed=1234, device=dev)
     times = []
     for i in range(a.warmup + a.steps):
-        secs, _, cores = cpu_oracle_sample(weights, x, lg, k, n)
+        secs, _, cores = cpu_oracle_sample(host, used, x, ids, wts, n)
         if i >= a.warmup:
             times.append(secs)
     secs = sum(times) / len(times)

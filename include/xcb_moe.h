@@ -69,7 +69,7 @@ typedef struct XcbMoeArgs {
   int32_t tokens;                 /* T (0 is allowed: nothing is launched)                      */
   int32_t top_k;                  /* routes per token, 1..16                                    */
   int32_t flags;                  /* XCB_FLAG_*                                                 */
-  int32_t reserved;
+  int32_t wait_limit_us;          /* bound of every device-side wait, microseconds (0: 2 s)     */
   const uint16_t* hidden_states;  /* bf16 [T, hidden], rows 16-byte aligned                     */
   const float* router_logits;     /* fp32 [T, total_experts] or NULL                            */
   const int32_t* topk_ids;        /* int32 [T, top_k] global ids, or NULL                       */
@@ -142,8 +142,16 @@ int xcb_moe_experts(const XcbMoeWeights* weights, const XcbMoeArgs* args, void* 
  * e.g. more than 31 tokens x top-8 at the DeepSeek-V3 shape) returns XCB_ERR_WORKSPACE before any launch.  The
  * function allocates nothing.  Its first call on a device looks up the array's device address (with that device
  * current) and caches it; make that first call before any stream capture.  All calls on a device share the one
- * array: calls that overlap on the GPU (other streams, other threads) race and must be serialised by the caller. */
+ * array: calls that overlap on the GPU (other streams, other threads) race and must be serialised by the caller.
+ * Device-side status bits (XCB_STATUS_*) of these calls stay in the array until xcb_moe_static_read_status reads
+ * them. */
 int xcb_moe_forward_static(const XcbMoeWeights* weights, const XcbMoeArgs* args, cudaStream_t stream);
+
+/* Status bits that xcb_moe_forward_static calls on the current device have set since the last read (a bounded wait
+ * that expired, an expert id out of range): synchronises `stream`, writes them to *device_status and clears them.
+ * Returns XCB_OK if none were set, XCB_ERR_DEVICE otherwise.  Like xcb_moe_forward_static it allocates nothing and
+ * has no counterpart in the reference. */
+int xcb_moe_static_read_status(int32_t* device_status, cudaStream_t stream);
 
 /* Synchronise `stream`, read the workspace status bits into *device_status, clear them.
  * Returns XCB_OK if none were set, XCB_ERR_DEVICE otherwise. */
@@ -158,14 +166,6 @@ int xcb_moe_read_status(void* workspace, int32_t* device_status, cudaStream_t st
  * status gets XCB_STATUS_DEVICE_TIMEOUT if a ring wait expired. */
 int xcb_hbm_probe(const void* src, size_t bytes, int mode, int chunk, int stages, int ctas_per_sm, int threads,
                   const long long* regions, int nreg, int32_t* status, float* sink, cudaStream_t stream);
-
-/* Tensor-pipe probe (diagnostic): one CTA per SM issues `chunks` x 4 back-to-back tcgen05.mma kind::f16
- * (M = 128, N = n, K = 16; A from tensor memory, or shared memory with a_smem != 0), cycling four A and four B
- * slots, with a tcgen05.commit after every `commit_every` chunks (a power of two; 0: none).  cycles[blockIdx]
- * (device, one per SM)
- * receives the clock cycles from the first issue to the completion of the last MMA. */
-int xcb_mma_probe(int a_smem, int n, int chunks, int commit_every, unsigned long long* cycles, int32_t* status,
-                  cudaStream_t stream);
 
 /* ---- expert parallelism ----
  * The reference models an expert-parallel rank only as a local expert range whose non-local routes are masked
@@ -207,7 +207,9 @@ int xcb_ep_combine(const uint16_t* parts, const int32_t* counts, const int32_t* 
  * order) every rank's rows are in this rank's buffer; the local layer then runs on them in place;
  * xcb_ep_p2p_combine sends partial rows
  * [d*T, (d+1)*T) to rank d and writes out bf16 [T, H] = sum over source ranks in rank order.  Every rank must make
- * the same calls in the same order.  Waits are bounded (2 s): status gets XCB_STATUS_DEVICE_TIMEOUT. */
+ * the same calls in the same order; T may change from step to step (up to T_max).  Waits are bounded by timeout_ns
+ * (0: 2 s): on timeout status gets XCB_STATUS_DEVICE_TIMEOUT and xcb_ep_p2p_combine writes NaN rows (also when the
+ * step's dispatch timed out), so a failed step cannot pass for a valid result. */
 size_t xcb_ep_p2p_bytes(int32_t G, int32_t T_max, int32_t H, int32_t k);
 int xcb_p2p_alloc(size_t bytes, void** ptr, void* handle);
 int xcb_p2p_open(const void* handle, void** ptr);
@@ -215,9 +217,10 @@ int xcb_p2p_close(void* ptr);
 int xcb_p2p_free(void* ptr);
 int xcb_ep_p2p_dispatch(const uint16_t* x, const float* logits, int32_t T, int32_t T_max, int32_t H, int32_t E,
                         int32_t k, int32_t G, int32_t rank, const uint64_t* peers, int32_t* status,
-                        cudaStream_t stream);
+                        uint64_t timeout_ns, cudaStream_t stream);
 int xcb_ep_p2p_combine(const uint16_t* parts, int32_t T, int32_t T_max, int32_t H, int32_t k, int32_t G,
-                       int32_t rank, const uint64_t* peers, uint16_t* out, int32_t* status, cudaStream_t stream);
+                       int32_t rank, const uint64_t* peers, uint16_t* out, int32_t* status, uint64_t timeout_ns,
+                       cudaStream_t stream);
 
 /* Quantise fp32 weights [E, R, K] to NVFP4 (gs = amax/(6*448) per expert, sf = e4m3(block_amax/6/gs),
  * codes RNE to E2M1): codes [E, R, K/2], sf [E, R, K/16], gs [E].  A utility for synthetic weights; the

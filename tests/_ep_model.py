@@ -93,3 +93,37 @@ def gloo_worker(rank, world, port, E, H, I, T, k, seed, result_dir):
         np.save(os.path.join(result_dir, f"ep_splits_{rank}.npy"), np.array(layer.last["send"] + layer.last["recv"]))
     finally:
         dist.destroy_process_group()
+
+
+def gloo_leave_worker(rank, world, port, E, H, I, T, k, seed, result_dir):
+    """Rank 1 runs one step and then leaves (returns between steps, with no collective in flight); rank 0 runs a
+    second step, whose first collective must end with an error once its peer is gone (the process group's short
+    timeout bounds it) instead of waiting for good.  Rank 0 writes what it saw."""
+    import datetime
+    import time
+
+    from xcalibur_b200.ep import ExpertParallelMoE
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    rng = np.random.default_rng(seed)
+    w = moe_ref.make_weights(rng, E, H, I)
+    epr = E // world
+    wl = [a[rank * epr:(rank + 1) * epr] for a in w]
+    layer = ExpertParallelMoE(*[torch.from_numpy(np.ascontiguousarray(a)) for a in wl], total_experts=E,
+                              _ops=CpuEpOps(wl, rank * epr))
+    x, logits = moe_ref.make_inputs(np.random.default_rng(seed + 1 + rank), T, H, E)
+    layer.forward(_from_bits(x), torch.from_numpy(logits), k)      # step 1 on both ranks
+    if rank == 1:
+        os._exit(0)                                              # leaves between steps, without a goodbye
+    t0 = time.monotonic()
+    try:
+        layer.forward(_from_bits(x), torch.from_numpy(logits), k)  # step 2: the peer is gone
+        msg = "step 2 completed without its peer"
+    except Exception as e:  # noqa: BLE001 - the failure is the expected outcome
+        msg = f"error after {time.monotonic() - t0:.1f} s: {type(e).__name__}"
+    with open(os.path.join(result_dir, "leave_0.txt"), "w") as f:
+        f.write(msg)
+    # the group cannot be torn down collectively any more; end the process without running its destructor
+    os._exit(0)

@@ -28,10 +28,10 @@ def test_bad_arguments_are_rejected_on_the_host():
     for args in [(0, 4, 64, 8, 2, 0, fake), (5, 4, 64, 8, 2, 0, fake), (1, 4, 60, 8, 2, 0, fake),
                  (1, 4, 64, 8, 2, 2, fake), (1, 4, 64, 8, 2, 0, None)]:
         T, Tm, H, k, G, rank, peers = args
-        assert lib.xcb_ep_p2p_dispatch(fake, fake, T, Tm, H, 256, k, G, rank, peers, fake, None) == \
+        assert lib.xcb_ep_p2p_dispatch(fake, fake, T, Tm, H, 256, k, G, rank, peers, fake, 0, None) == \
             _lib.XCB_ERR_INVALID_ARG
-        assert lib.xcb_ep_p2p_combine(fake, T, Tm, H, k, G, rank, peers, fake, fake, None) == \
+        assert lib.xcb_ep_p2p_combine(fake, T, Tm, H, k, G, rank, peers, fake, fake, 0, None) == \
             _lib.XCB_ERR_INVALID_ARG
-    assert lib.xcb_ep_p2p_dispatch(fake, fake, 1, 4, 64, 513, 8, 2, 0, fake, fake, None) == _lib.XCB_ERR_INVALID_ARG
+    assert lib.xcb_ep_p2p_dispatch(fake, fake, 1, 4, 64, 513, 8, 2, 0, fake, fake, 0, None) == _lib.XCB_ERR_INVALID_ARG
     assert lib.xcb_p2p_alloc(0, ctypes.byref(ctypes.c_void_p()), None) == _lib.XCB_ERR_INVALID_ARG
     assert lib.xcb_p2p_open(None, ctypes.byref(ctypes.c_void_p())) == _lib.XCB_ERR_INVALID_ARG

@@ -38,18 +38,20 @@ def test_ep_two_gpus_match_single_gpu(tmp_path, T, p2p, calls):
         assert_close_bf16(torch.from_numpy(got.view(np.int16)).view(torch.bfloat16), want)
 
 
-def test_p2p_exchange_one_rank_round_trip(cuda_device):
-    """The peer-exchange kernels on one rank (its buffer is its only peer; one block per peer, so each kernel
-    raises the flag it then waits for): the received rows equal what was sent, the received top-k rows equal the
-    library router's on the same logits, the combine returns the partial rows summed over the one rank, and three
-    consecutive steps keep the per-step flags in step."""
+@pytest.mark.parametrize("Tm,H,E,k,steps", [(4, 256, 64, 4, (3, 1, 4)), (32, 7168, 256, 8, (2, 32, 1, 7))])
+def test_p2p_exchange_one_rank_round_trip(cuda_device, Tm, H, E, k, steps):
+    """The peer-exchange kernels on one rank (its buffer is its only peer, so each kernel raises the flags it then
+    waits for): the received rows equal what was sent, the received top-k rows equal the library router's on the
+    same logits, the combine returns the partial rows summed over the one rank, and consecutive steps keep the
+    flags in step.  At H = 7168 and T_max = 32 several blocks push to each peer, and steps of 2, 32, 1 and 7
+    tokens leave some of them with no rows: the flags' targets must not depend on a step's size."""
     import ctypes
 
     from xcalibur_b200 import _lib
     from xcalibur_b200.ep import _DeviceBytes, p2p_layout
 
     lib = _lib.load()
-    G, Tm, H, E, k = 1, 4, 256, 64, 4
+    G = 1
     nbytes = lib.xcb_ep_p2p_bytes(G, Tm, H, k)
     own = ctypes.c_void_p()
     handle = (ctypes.c_ubyte * 64)()
@@ -61,14 +63,14 @@ def test_p2p_exchange_one_rank_round_trip(cuda_device):
         status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
         stream = torch.cuda.current_stream(cuda_device).cuda_stream
         g = torch.Generator(device=cuda_device).manual_seed(5)
-        for step, T in enumerate((3, 1, 4)):
+        for step, T in enumerate(steps):
             x = torch.randn((T, H), generator=g, device=cuda_device).to(torch.bfloat16)
             logits = torch.randn((T, E), generator=g, device=cuda_device)
             ids = torch.empty((T, k), dtype=torch.int32, device=cuda_device)
             wts = torch.empty((T, k), dtype=torch.float32, device=cuda_device)
             assert lib.xcb_moe_topk(logits.data_ptr(), T, E, k, ids.data_ptr(), wts.data_ptr(), stream) == _lib.XCB_OK
             assert lib.xcb_ep_p2p_dispatch(x.data_ptr(), logits.data_ptr(), T, Tm, H, E, k, G, 0, peers.data_ptr(),
-                                           status.data_ptr(), stream) == _lib.XCB_OK
+                                           status.data_ptr(), 0, stream) == _lib.XCB_OK
             parts = torch.randn((T, H), generator=g, device=cuda_device).to(torch.bfloat16)
             out = torch.empty((T, H), dtype=torch.bfloat16, device=cuda_device)
             torch.cuda.synchronize(cuda_device)
@@ -76,7 +78,7 @@ def test_p2p_exchange_one_rank_round_trip(cuda_device):
             ids_r = buf[io:io + T * k * 4].view(torch.int32).view(T, k).clone()
             w_r = buf[wo:wo + T * k * 4].view(torch.float32).view(T, k).clone()
             assert lib.xcb_ep_p2p_combine(parts.data_ptr(), T, Tm, H, k, G, 0, peers.data_ptr(), out.data_ptr(),
-                                          status.data_ptr(), stream) == _lib.XCB_OK
+                                          status.data_ptr(), 0, stream) == _lib.XCB_OK
             torch.cuda.synchronize(cuda_device)
             assert int(status.item()) == 0, f"step {step}: device status {int(status.item())}"
             assert torch.equal(xr, x)
@@ -97,3 +99,46 @@ def test_p2p_exchange_set_up_on_one_rank(tmp_path, cuda_device):
     with open(os.path.join(tmp_path, "p2p_single.txt")) as f:
         msg = f.read()
     assert msg == "", msg
+
+
+def test_p2p_wait_for_a_silent_peer_runs_out(cuda_device):
+    """Rank 0 of a two-rank exchange whose rank 1 never sends (its 'buffer' is a second local allocation that no
+    kernel writes to rank 0): the dispatch's wait for rank 1's rows and the combine's wait for its partial sums give
+    up after the 1 ms limit, the status word reports XCB_STATUS_DEVICE_TIMEOUT, both kernels return (the stream
+    synchronises) and the combine's output is NaN rows, not a plausible result.  Nothing but the wait's own limit is
+    exercised: every access stays inside the two allocations."""
+    import ctypes
+
+    from xcalibur_b200 import _lib
+
+    lib = _lib.load()
+    G, Tm, H, E, k, T = 2, 4, 256, 64, 4, 3
+    nbytes = lib.xcb_ep_p2p_bytes(G, Tm, H, k)
+    bufs = []
+    try:
+        for _ in range(G):
+            p = ctypes.c_void_p()
+            assert lib.xcb_p2p_alloc(nbytes, ctypes.byref(p), (ctypes.c_ubyte * 64)()) == _lib.XCB_OK
+            bufs.append(p)
+        peers = torch.tensor([b.value for b in bufs], dtype=torch.int64, device=cuda_device)
+        status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+        stream = torch.cuda.current_stream(cuda_device).cuda_stream
+        x = torch.randn((T, H), device=cuda_device).to(torch.bfloat16)
+        logits = torch.randn((T, E), device=cuda_device)
+        limit_ns = 1_000_000
+        assert lib.xcb_ep_p2p_dispatch(x.data_ptr(), logits.data_ptr(), T, Tm, H, E, k, G, 0, peers.data_ptr(),
+                                       status.data_ptr(), limit_ns, stream) == _lib.XCB_OK
+        torch.cuda.synchronize(cuda_device)
+        assert int(status.item()) & _lib.XCB_STATUS_DEVICE_TIMEOUT
+        status.zero_()
+        parts = torch.ones((G * T, H), dtype=torch.bfloat16, device=cuda_device)
+        out = torch.zeros((T, H), dtype=torch.bfloat16, device=cuda_device)
+        assert lib.xcb_ep_p2p_combine(parts.data_ptr(), T, Tm, H, k, G, 0, peers.data_ptr(), out.data_ptr(),
+                                      status.data_ptr(), limit_ns, stream) == _lib.XCB_OK
+        torch.cuda.synchronize(cuda_device)
+        assert int(status.item()) & _lib.XCB_STATUS_DEVICE_TIMEOUT
+        assert torch.isnan(out.float()).all()
+    finally:
+        torch.cuda.synchronize(cuda_device)
+        for b in bufs:
+            lib.xcb_p2p_free(b)

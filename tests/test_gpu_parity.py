@@ -337,3 +337,18 @@ def test_activations_beyond_f16_range(dev, T, path):
     assert np.isfinite(got).all()
     scale = np.abs(ref).max()
     assert np.abs(got - ref).max() <= 1e-2 * scale
+
+
+def test_bench_reference_arm_experts_match_library(dev):
+    """bench.py's reference arm builds its experts without this repository's CUDA library (same fp32 draws,
+    quantised on the host by the CPU oracle); they must equal the library-built layer byte for byte, so both arms
+    time the same layer."""
+    import bench
+    from xcalibur_b200 import synth
+
+    cfg = dict(E=12, H=512, I=256)
+    full = synth.make_weights(cfg["E"], cfg["H"], cfg["I"], seed=99, device=dev)
+    used = np.array([0, 5, 8, 11])
+    host = bench.reference_arm_experts(cfg, used, seed=99, device=dev)
+    for name in ("w13", "w13_sf", "w13_gs", "w2", "w2_sf", "w2_gs"):
+        assert np.array_equal(host[name], to_np(full[name][torch.as_tensor(used, device=dev)])), name

@@ -70,5 +70,7 @@ def test_forward_rejects_bad_arguments_before_launch():
     assert lib.xcb_moe_forward(ctypes.byref(w), ctypes.byref(a), 16, 1 << 30, None) == _lib.XCB_ERR_INVALID_ARG
     a = _lib.XcbMoeArgs(4, 2, _lib.XCB_FLAG_POST_NORM, 0, 16, 16, None, None, 16, None, None)  # no post_norm_w
     assert lib.xcb_moe_forward(ctypes.byref(w), ctypes.byref(a), 16, 1 << 30, None) == _lib.XCB_ERR_INVALID_ARG
+    a = _lib.XcbMoeArgs(4, 2, 0, -1, 16, 16, None, None, 16, None, None)     # negative wait limit
+    assert lib.xcb_moe_forward(ctypes.byref(w), ctypes.byref(a), 16, 1 << 30, None) == _lib.XCB_ERR_INVALID_ARG
     a = _lib.XcbMoeArgs(0, 2, 0, 0, 16, 16, None, None, 16, None, None)      # T = 0: nothing to do
     assert lib.xcb_moe_forward(ctypes.byref(w), ctypes.byref(a), 16, 0, None) == _lib.XCB_OK

@@ -42,10 +42,10 @@ EXPORTS = (
     "xcb_moe_route",
     "xcb_moe_experts",
     "xcb_moe_forward_static",
+    "xcb_moe_static_read_status",
     "xcb_moe_read_status",
     "xcb_nvfp4_quantize",
     "xcb_hbm_probe",
-    "xcb_mma_probe",
     "xcb_moe_topk",
     "xcb_ep_plan",
     "xcb_ep_gather",
@@ -72,7 +72,7 @@ class XcbMoeWeights(ctypes.Structure):
 
 class XcbMoeArgs(ctypes.Structure):
     _fields_ = [("tokens", ctypes.c_int32), ("top_k", ctypes.c_int32), ("flags", ctypes.c_int32),
-                ("reserved", ctypes.c_int32), ("hidden_states", ctypes.c_void_p), ("router_logits", ctypes.c_void_p),
+                ("wait_limit_us", ctypes.c_int32), ("hidden_states", ctypes.c_void_p), ("router_logits", ctypes.c_void_p),
                 ("topk_ids", ctypes.c_void_p), ("topk_weights", ctypes.c_void_p), ("out", ctypes.c_void_p),
                 ("topk_ids_out", ctypes.c_void_p), ("topk_weights_out", ctypes.c_void_p)]
 
@@ -88,7 +88,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     if not os.path.exists(path):
         raise OSError(f"{path} is missing: run `python -m xcalibur_b200.build` (or __graft_entry__.build())")
     lib = ctypes.CDLL(path)
-    P, I32, SZ = ctypes.c_void_p, ctypes.c_int32, ctypes.c_size_t
+    P, I32, SZ, U64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_size_t, ctypes.c_uint64
     sig = {
         "xcb_status_str": (ctypes.c_char_p, [ctypes.c_int]),
         "xcb_moe_check_shape": (ctypes.c_int, [ctypes.POINTER(XcbMoeShape)]),
@@ -103,10 +103,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "xcb_moe_experts": (ctypes.c_int, [ctypes.POINTER(XcbMoeWeights), ctypes.POINTER(XcbMoeArgs), P, SZ, P]),
         "xcb_moe_forward_static": (ctypes.c_int, [ctypes.POINTER(XcbMoeWeights), ctypes.POINTER(XcbMoeArgs), P]),
         "xcb_moe_read_status": (ctypes.c_int, [P, ctypes.POINTER(I32), P]),
+        "xcb_moe_static_read_status": (ctypes.c_int, [ctypes.POINTER(I32), P]),
         "xcb_nvfp4_quantize": (ctypes.c_int, [P, I32, I32, I32, P, P, P, P, P]),
         "xcb_hbm_probe": (ctypes.c_int, [P, SZ, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                          P, ctypes.c_int, P, P, P]),
-        "xcb_mma_probe": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P]),
         "xcb_moe_topk": (ctypes.c_int, [P, I32, I32, I32, P, P, P]),
         "xcb_ep_plan": (ctypes.c_int, [P, I32, I32, I32, I32, P, P, P, P, P]),
         "xcb_ep_p2p_bytes": (SZ, [I32, I32, I32, I32]),
@@ -114,8 +114,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "xcb_p2p_open": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_void_p)]),
         "xcb_p2p_close": (ctypes.c_int, [P]),
         "xcb_p2p_free": (ctypes.c_int, [P]),
-        "xcb_ep_p2p_dispatch": (ctypes.c_int, [P, P, I32, I32, I32, I32, I32, I32, I32, P, P, P]),
-        "xcb_ep_p2p_combine": (ctypes.c_int, [P, I32, I32, I32, I32, I32, I32, P, P, P, P]),
+        "xcb_ep_p2p_dispatch": (ctypes.c_int, [P, P, I32, I32, I32, I32, I32, I32, I32, P, P, U64, P]),
+        "xcb_ep_p2p_combine": (ctypes.c_int, [P, I32, I32, I32, I32, I32, I32, P, P, P, U64, P]),
         "xcb_ep_gather": (ctypes.c_int, [P, P, P, I32, I32, I32, I32, P, P, P, P, P, P]),
         "xcb_ep_combine": (ctypes.c_int, [P, P, P, I32, I32, I32, P, P]),
     }

@@ -11,7 +11,7 @@
 using namespace xcb;
 
 namespace {
-constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per bounded wait
+constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per bounded wait unless the call sets its own
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
@@ -110,7 +110,9 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   int rc = shape_ok(s);
   if (rc != XCB_OK) return rc;
   if (a->tokens < 0 || a->top_k <= 0 || a->top_k > 16 || a->top_k > s->total_experts) return XCB_ERR_INVALID_ARG;
+  if (a->wait_limit_us < 0) return XCB_ERR_INVALID_ARG;
   if (a->tokens == 0) return XCB_OK;
+  const unsigned long long timeout_ns = a->wait_limit_us ? (unsigned long long)a->wait_limit_us * 1000ull : kTimeoutNs;
   if (!a->hidden_states || !a->out || !w->gate_up || !w->down || !w->gate_up_gs || !w->down_gs)
     return XCB_ERR_INVALID_ARG;
   const bool have_logits = a->router_logits != nullptr;
@@ -205,7 +207,7 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   }
   sp->post_norm = post_norm ? 1 : 0;
   sp->grid_combine = (post_norm || !small) ? 1 : 0;
-  sp->timeout_ns = kTimeoutNs;
+  sp->timeout_ns = timeout_ns;
 
   WidePathParams* wp = &plan->wp;
   *wp = WidePathParams{};
@@ -232,7 +234,7 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   wp->I = s->inter;
   wp->E_loc = s->num_experts;
   wp->post_norm = post_norm ? 1 : 0;
-  wp->timeout_ns = kTimeoutNs;
+  wp->timeout_ns = timeout_ns;
   return XCB_OK;
 }
 
@@ -304,10 +306,19 @@ int xcb_moe_forward_static(const XcbMoeWeights* w, const XcbMoeArgs* a, cudaStre
   void* ws = nullptr;
   rc = static_scratch_address(&ws);
   if (rc != XCB_OK) return rc;
-  // The array keeps the previous call's contents: clear the control words (status bits and counters) that the
-  // kernels expect to start at zero; every other region is rewritten by the call before it is read.
-  if (cudaMemsetAsync(ws, 0, kCtlWords * sizeof(int), stream) != cudaSuccess) return XCB_ERR_CUDA;
+  // The array keeps the previous call's contents: clear the control words (counters) that the kernels expect to
+  // start at zero; every other region is rewritten by the call before it is read.  Word 0, the status bits, is
+  // kept, so device errors of earlier calls accumulate until xcb_moe_static_read_status reads and clears them.
+  if (cudaMemsetAsync((int*)ws + 1, 0, (kCtlWords - 1) * sizeof(int), stream) != cudaSuccess) return XCB_ERR_CUDA;
   return xcb_moe_forward(w, a, ws, (size_t)XCB_STATIC_SCRATCH_BYTES, stream);
+}
+
+int xcb_moe_static_read_status(int32_t* device_status, cudaStream_t stream) {
+  if (!device_status) return XCB_ERR_INVALID_ARG;
+  void* ws = nullptr;
+  const int rc = static_scratch_address(&ws);
+  if (rc != XCB_OK) return rc;
+  return xcb_moe_read_status(ws, device_status, stream);
 }
 
 int xcb_moe_read_status(void* ws, int32_t* device_status, cudaStream_t stream) {

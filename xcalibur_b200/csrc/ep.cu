@@ -225,8 +225,11 @@ int xcb_ep_combine(const uint16_t* parts, const int32_t* counts, const int32_t* 
 // their top-k row (written by d) and a slot for the partial sums this rank's tokens got on d (written by d).
 // dispatch: push this rank's rows into slot [rank] of every peer, fence, raise the peer's x flag; wait until every
 // peer has raised this rank's.  combine: push each peer's partial rows into slot [rank] of that peer, fence, raise
-// its part flag; wait for all; out = bf16(sum over d in rank order).  Flags count block arrivals and only grow
-// (epoch e of this rank: e * blocks per peer), so no reset is needed between steps; every wait is bounded.
+// its part flag; wait for all; out = bf16(sum over d in rank order).  Flags count block arrivals and only grow: the
+// number of pushing blocks per peer (nb) depends on the buffer's T_max alone, never on a step's T (a block whose
+// share of a small step is empty still raises its flag), so after e steps every flag of a rank stands at e * nb and
+// no reset is needed between steps of any size.  Every wait is bounded; on timeout the status word gets
+// XCB_STATUS_DEVICE_TIMEOUT and the combine writes NaN rows, so a failed step cannot pass for a valid result.
 namespace xcb {
 
 struct P2pLayout {
@@ -330,9 +333,18 @@ __global__ void ep_p2p_combine_kernel(const uint16_t* __restrict__ parts, int T,
   if (threadIdx.x == 0) {
     p2p_red_release(reinterpret_cast<unsigned*>(dst + L.flag) + G + rank, 1u);
     ok = p2p_wait_all(reinterpret_cast<const unsigned*>(mine + L.flag) + G, G, e * (unsigned)nb, timeout_ns, status);
+    // a dispatch of this step that timed out left the local layer with incomplete rows: the sums are invalid too
+    if (*reinterpret_cast<volatile int*>(status) & XCB_STATUS_DEVICE_TIMEOUT) ok = 0;
   }
   __syncthreads();
-  if (ok) {
+  if (!ok) {
+    // NaN rows instead of stale or partial sums (bf16 quiet NaN 0x7FC0)
+    const int nq = T * (H / 4);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nq; i += gridDim.x * blockDim.x) {
+      const int t = i / (H / 4), c = (i % (H / 4)) * 4;
+      *reinterpret_cast<uint2*>(out + (size_t)t * H + c) = make_uint2(0x7FC07FC0u, 0x7FC07FC0u);
+    }
+  } else {
     // out = bf16(sum over source ranks in rank order), this block's slice of the T x H outputs
     const uint16_t* pin = reinterpret_cast<const uint16_t*>(mine + L.part);
     const int nq = T * (H / 4);
@@ -404,36 +416,41 @@ int xcb_p2p_free(void* ptr) {
   return cudaFree(ptr) == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
 }
 
-static int p2p_blocks(int T, int H) {
-  const long long bytes = (long long)T * H * 2;
+// Pushing blocks per peer for a buffer of T_max rows per rank (about 64 KB of rows each).  It must not depend on
+// a step's T: the flags' targets are (steps so far) x nb.
+static int p2p_blocks(int T_max, int H) {
+  const long long bytes = (long long)T_max * H * 2;
   long long nb = (bytes + kP2pRowBytesPerBlock - 1) / kP2pRowBytesPerBlock;
   nb = nb < 1 ? 1 : nb;
-  return (int)(nb > T ? T : nb);
+  return (int)(nb > T_max ? T_max : nb);
 }
+
+static uint64_t p2p_timeout(uint64_t timeout_ns) { return timeout_ns ? timeout_ns : 2000000000ull; }
 
 int xcb_ep_p2p_dispatch(const uint16_t* x, const float* logits, int32_t T, int32_t T_max, int32_t H, int32_t E,
                         int32_t k, int32_t G, int32_t rank, const uint64_t* peers, int32_t* status,
-                        cudaStream_t stream) {
+                        uint64_t timeout_ns, cudaStream_t stream) {
   if (T <= 0 || T > T_max || H <= 0 || H % 8 || E <= 0 || E > 512 || k <= 0 || k > 16 || k > E || G <= 0 ||
       G > kEpMaxRanks || rank < 0 || rank >= G)
     return XCB_ERR_INVALID_ARG;
   if (!x || !logits || !peers || !status || ((uintptr_t)x & 15u)) return XCB_ERR_INVALID_ARG;
-  const int nb = p2p_blocks(T, H);
+  const int nb = p2p_blocks(T_max, H);
   ep_p2p_dispatch_kernel<<<G * nb, 256, 0, stream>>>(x, logits, T, T_max, H, E, k, G, rank, peers, nb,
-                                                     p2p_layout(G, T_max, H, k), 2000000000ull, status);
+                                                     p2p_layout(G, T_max, H, k), p2p_timeout(timeout_ns), status);
   return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
 }
 
 int xcb_ep_p2p_combine(const uint16_t* parts, int32_t T, int32_t T_max, int32_t H, int32_t k, int32_t G,
-                       int32_t rank, const uint64_t* peers, uint16_t* out, int32_t* status, cudaStream_t stream) {
+                       int32_t rank, const uint64_t* peers, uint16_t* out, int32_t* status, uint64_t timeout_ns,
+                       cudaStream_t stream) {
   if (T <= 0 || T > T_max || H <= 0 || H % 8 || k <= 0 || k > 16 || G <= 0 || G > kEpMaxRanks || rank < 0 ||
       rank >= G)
     return XCB_ERR_INVALID_ARG;
   if (!parts || !peers || !out || !status || ((uintptr_t)parts & 15u) || ((uintptr_t)out & 7u))
     return XCB_ERR_INVALID_ARG;
-  const int nb = p2p_blocks(T, H);
+  const int nb = p2p_blocks(T_max, H);
   ep_p2p_combine_kernel<<<G * nb, 256, 0, stream>>>(parts, T, T_max, H, G, rank, peers, nb,
-                                                    p2p_layout(G, T_max, H, k), out, 2000000000ull, status);
+                                                    p2p_layout(G, T_max, H, k), out, p2p_timeout(timeout_ns), status);
   return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
 }
 

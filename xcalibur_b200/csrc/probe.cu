@@ -9,13 +9,7 @@
 // Every CTA streams a contiguous share of `bytes`.  Reference counterpart: the BW_SRC bulk-copy probes of
 // kernels/moe_w4a16_h200/moe_w4a16.py:2890-3061 (dead code there); here they measure the roofline denominators
 // and the ring shapes the decode kernel is sized from.
-//
-// The tensor-pipe probe (xcb_mma_probe) times back-to-back tcgen05.mma kind::f16 (M = 128, K = 16) the way the
-// prefill kernel issues them: 64-k chunks of four MMAs cycling four A and four B slots, A from tensor memory or
-// shared memory, with a tcgen05.commit after every `commit_every` chunks (a power of two; 0: none); one CTA per SM,
-// cycles per CTA.
 #include "common.cuh"
-#include "tcgen05.cuh"
 
 namespace xcb {
 
@@ -99,95 +93,9 @@ __global__ void __launch_bounds__(1024) probe_kernel(ProbeParams p) {
   }
 }
 
-constexpr int kMpA = 4 * 16384, kMpB = 4 * 32768;  // four A slots (128 x 64 bf16), four B slots (256 x 64 bf16)
-
-__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
-      : "memory");
-}
-
-__global__ void __launch_bounds__(128, 1) mma_probe_kernel(int a_smem, int n, int chunks, int commit_every,
-                                                           unsigned long long* cycles, int* status) {
-  extern __shared__ uint8_t mp_raw[];
-  uint8_t* sm = mp_raw + ((1024u - (smem_u32(mp_raw) & 1023u)) & 1023u);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kMpA + kMpB);  // [0]: per-window commits, [1]: the final one
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 2);
-  const int warp = threadIdx.x >> 5;
-  for (int i = threadIdx.x; i < (kMpA + kMpB) / 16; i += blockDim.x)  // operand values do not matter
-    reinterpret_cast<uint4*>(sm)[i] = make_uint4(0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u);
-  if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
-    mbar_init(bar + 1, 1);
-    fence_mbar_init();
-  }
-  if (warp == 0) {
-    tmem_alloc(tslot, 512);
-    tmem_relinquish();
-  }
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tslot;
-  if (warp == 0) {
-    const uint32_t idesc = idesc_bf16_m128(n);
-    const uint64_t ad0 = sdesc_sw128(smem_u32(sm)), bd0 = sdesc_sw128(smem_u32(sm + kMpA));
-    const unsigned long long t0 = clock64();
-    for (int c = 0; c < chunks; ++c) {
-      const uint32_t s = c & 3;
-      if (elect_one()) {
-        const uint64_t bd = bd0 + (uint64_t)(s * (32768 >> 4));
-        if (!a_smem) {
-          const uint32_t ta = tmem + s * 32;  // A ring in columns [0, 128), D from column 128
-          tc_mma_ts(tmem + 128, ta, bd, idesc, c > 0);
-          tc_mma_ts(tmem + 128, ta + 8, bd + 2, idesc, 1u);
-          tc_mma_ts(tmem + 128, ta + 16, bd + 4, idesc, 1u);
-          tc_mma_ts(tmem + 128, ta + 24, bd + 6, idesc, 1u);
-        } else {
-          const uint64_t ad = ad0 + (uint64_t)(s * (16384 >> 4));
-          mma_ss(tmem + 128, ad, bd, idesc, c > 0);
-          mma_ss(tmem + 128, ad + 2, bd + 2, idesc, 1u);
-          mma_ss(tmem + 128, ad + 4, bd + 4, idesc, 1u);
-          mma_ss(tmem + 128, ad + 6, bd + 6, idesc, 1u);
-        }
-        if (commit_every && (c & (commit_every - 1)) == commit_every - 1) tc_commit(bar);
-      }
-      __syncwarp();
-    }
-    if (elect_one()) tc_commit(bar + 1);  // completes once every MMA above has
-    __syncwarp();
-    mbar_wait(bar + 1, 0, 2000000000ull, status);
-    if (threadIdx.x == 0) cycles[blockIdx.x] = clock64() - t0;
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
 }  // namespace xcb
 
 using namespace xcb;
-
-extern "C" int xcb_mma_probe(int a_smem, int n, int chunks, int commit_every, unsigned long long* cycles,
-                             int32_t* status, cudaStream_t stream) {
-  if (!cycles || !status || n < 16 || n > 256 || n % 16 || chunks < 1 || commit_every < 0 ||
-      (commit_every & (commit_every - 1)))
-    return XCB_ERR_INVALID_ARG;
-  int dev = 0, sms = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    return XCB_ERR_CUDA;
-  const int smem = kMpA + kMpB + 64 + 1024;
-  if (cudaFuncSetAttribute(mma_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return XCB_ERR_CUDA;
-  mma_probe_kernel<<<sms, 128, smem, stream>>>(a_smem, n, chunks, commit_every, cycles, status);
-  return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
-}
 
 extern "C" int xcb_hbm_probe(const void* src, size_t bytes, int mode, int chunk, int stages, int ctas_per_sm,
                              int threads, const long long* regions, int nreg, int32_t* status, float* sink,

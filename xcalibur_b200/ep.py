@@ -75,8 +75,10 @@ class P2PExchange:
     and a one-step self-test are checked by all ranks together) and must ``close`` it before the process group is
     destroyed.  Raises ``P2PUnavailable`` on every rank if any rank failed, after releasing what it set up."""
 
-    def __init__(self, lib, group, rank: int, world: int, T_max: int, H: int, E: int, k: int, device):
+    def __init__(self, lib, group, rank: int, world: int, T_max: int, H: int, E: int, k: int, device,
+                 timeout_ns: int = 0):
         self.lib, self.group, self.rank, self.world = lib, group, rank, world
+        self.timeout_ns = int(timeout_ns)  # bound of every device wait of the exchange (0: the library's 2 s)
         self.T_max, self.H, self.E, self.k, self.device = T_max, H, E, k, device
         self.offs = p2p_layout(world, T_max, H, k)
         nbytes = int(lib.xcb_ep_p2p_bytes(world, T_max, H, k))
@@ -179,17 +181,18 @@ class P2PExchange:
         stream = torch.cuda.current_stream(self.device).cuda_stream
         check(self.lib.xcb_ep_p2p_dispatch(x.data_ptr(), logits.data_ptr(), T, self.T_max, self.H, self.E, self.k,
                                            self.world, self.rank, self.peers.data_ptr(), self.status.data_ptr(),
-                                           stream), "xcb_ep_p2p_dispatch")
+                                           self.timeout_ns, stream), "xcb_ep_p2p_dispatch")
 
     def combine(self, parts, T: int):
         out = torch.empty((T, self.H), dtype=torch.bfloat16, device=self.device)
         stream = torch.cuda.current_stream(self.device).cuda_stream
         check(self.lib.xcb_ep_p2p_combine(parts.data_ptr(), T, self.T_max, self.H, self.k, self.world, self.rank,
-                                          self.peers.data_ptr(), out.data_ptr(), self.status.data_ptr(), stream),
-              "xcb_ep_p2p_combine")
+                                          self.peers.data_ptr(), out.data_ptr(), self.status.data_ptr(),
+                                          self.timeout_ns, stream), "xcb_ep_p2p_combine")
         return out
 
     def device_status(self) -> int:
+        """Status bits of the exchange kernels (XCB_STATUS_DEVICE_TIMEOUT), read and cleared (synchronises)."""
         v = int(self.status.item())
         self.status.zero_()
         return v
@@ -304,6 +307,17 @@ class ExpertParallelMoE:
             except P2PUnavailable as e:  # every rank lands here together: the dense step falls back to NCCL
                 self.p2p_error = str(e)
 
+    def device_status(self) -> int:
+        """Device status bits of this rank's last steps (exchange waits that timed out, expert ids out of range,
+        the local layer's own bits), read and cleared.  It synchronises, so a serving loop calls it between steps
+        rather than inside one; a step whose exchange timed out has NaN output rows in any case."""
+        bits = 0
+        if self.p2p is not None:
+            bits |= self.p2p.device_status()
+        if isinstance(self.ops, CudaEpOps):
+            bits |= self.ops.device_status() | self.ops.layer.check_device_status()
+        return bits
+
     def close(self):
         """Release the peer exchange (collective; before the process group is destroyed)."""
         if self.p2p is not None:
@@ -331,8 +345,9 @@ class ExpertParallelMoE:
         parts = self.ops.local(xr, ids_r, w_r, self.post_norm)
         out = ex.combine(parts, T)
         mine = slice(self.rank * T, (self.rank + 1) * T)
-        self.last.update({"ids": ids_r[mine], "wts": w_r[mine], "send": [T] * self.world, "recv": [T] * self.world,
-                          "recv_ids": ids_r})
+        # copies: the receive buffer is rewritten by the peers' next dispatch
+        self.last.update({"ids": ids_r[mine].clone(), "wts": w_r[mine].clone(), "send": [T] * self.world,
+                          "recv": [T] * self.world, "recv_ids": ids_r.clone()})
         return out
 
     def _dense(self, x, ids, wts, top_k):

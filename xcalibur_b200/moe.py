@@ -158,11 +158,12 @@ class PreparedMoE:
     def build_call(self, hidden_states: torch.Tensor, router_logits: Optional[torch.Tensor] = None, top_k: int = 8,
                    *, topk_ids: Optional[torch.Tensor] = None, topk_weights: Optional[torch.Tensor] = None,
                    post_norm: bool = False, out: Optional[torch.Tensor] = None, return_routing: bool = False,
-                   path: str = "auto"):
+                   path: str = "auto", wait_limit_us: int = 0):
         """Validate one call and bind its buffers; returns a ``LayerCall`` whose ``launch()`` enqueues it.
 
         ``path``: "auto" (the library picks by batch size), "decode" (the streaming decode kernel) or "prefill"
-        (the tensor-core grouped GEMMs)."""
+        (the tensor-core grouped GEMMs).  ``wait_limit_us``: bound of every device-side wait of the call (0: the
+        library's 2 s); a wait that runs out sets XCB_STATUS_DEVICE_TIMEOUT (``check_device_status``)."""
         x = hidden_states
         if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != self.H:
             raise ValueError(f"hidden_states must be bf16 [T, {self.H}]")
@@ -197,7 +198,9 @@ class PreparedMoE:
         if path not in _PATH_FLAGS:
             raise ValueError(f"path must be one of {sorted(_PATH_FLAGS)}")
         flags = (_lib.XCB_FLAG_POST_NORM if post_norm else 0) | _PATH_FLAGS[path]
-        args = XcbMoeArgs(T, top_k, flags, 0, x.data_ptr(), _ptr(logits),
+        if wait_limit_us < 0:
+            raise ValueError("wait_limit_us must be >= 0")
+        args = XcbMoeArgs(T, top_k, flags, int(wait_limit_us), x.data_ptr(), _ptr(logits),
                           _ptr(ids), _ptr(wts), out.data_ptr(), _ptr(ids_out), _ptr(wts_out))
         return LayerCall(self, args, ws, (x, logits, ids, wts), out, ids_out, wts_out, return_routing)
 

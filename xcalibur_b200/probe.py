@@ -1,6 +1,4 @@
-"""HBM read-bandwidth sweep on the current GPU (``python -m xcalibur_b200.probe``); ``--mma`` instead times the
-tensor pipe the way the prefill kernel issues it (clocks per M=128, K=16 MMA, by N, A operand source and commit
-cadence).
+"""HBM read-bandwidth sweep on the current GPU (``python -m xcalibur_b200.probe``).
 
 Runs ``xcb_hbm_probe`` over a few ring shapes and prints one JSON line per shape: the bulk-copy ring the decode
 kernel uses (chunk x stages per CTA, with and without the L2 evict-first hint, 1 or 2 CTAs per SM) and plain
@@ -50,12 +48,9 @@ def main():
     ap.add_argument("--windows", default="", help="comma-separated MiB per launch (rotating offsets), e.g. 66,132,512")
     ap.add_argument("--l2-mb", type=int, default=0,
                     help="L2 read bandwidth instead: every CTA streams the same L2-resident block of this many MiB")
-    ap.add_argument("--mma", action="store_true", help="tensor-pipe probe instead (clocks per MMA)")
     a = ap.parse_args()
     if a.l2_mb:
         return l2_sweep(a.l2_mb)
-    if a.mma:
-        return mma_sweep()
     buf = torch.empty(int(a.gib * (1 << 30)), dtype=torch.uint8, device="cuda")
     buf.random_(0, 255)
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
@@ -111,28 +106,6 @@ def l2_sweep(mb: int):
             best = ms if best is None else min(best, ms)
         print(json.dumps({"mode": "l2_bulk_ring", "block_mb": mb, "chunk": chunk, "stages": stages, "ctas_per_sm": ctas,
                           "gbs": round(total / (best * 1e-3) / 1e9, 1), "status": int(status.item())}), flush=True)
-
-
-def mma_sweep(chunks: int = 4096):
-    """Clocks per tcgen05.mma (M = 128, K = 16) issued in 64-k chunks of four, by N, A source and commit cadence;
-    the model column is max(44, N / 2), the back-to-back rate."""
-    lib = _lib.load()
-    sms = torch.cuda.get_device_properties(0).multi_processor_count
-    cycles = torch.zeros(sms, dtype=torch.int64, device="cuda")
-    status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    stream = torch.cuda.current_stream().cuda_stream
-    for a_smem in (0, 1):
-        for commit_every in (1, 2, 4, 16, 0):
-            for n in (32, 64, 96, 128, 192, 256):
-                for _ in range(2):  # the second launch is timed warm
-                    _lib.check(lib.xcb_mma_probe(a_smem, n, chunks, commit_every, cycles.data_ptr(),
-                                                 status.data_ptr(), stream), "xcb_mma_probe")
-                torch.cuda.synchronize()
-                c = cycles.double() / (4 * chunks)
-                print(json.dumps({"mode": "mma_probe", "a_operand": "smem" if a_smem else "tmem", "n": n,
-                                  "commit_every_chunks": commit_every, "clk_per_mma_mean": round(c.mean().item(), 1),
-                                  "clk_per_mma_max": round(c.max().item(), 1), "model": max(44, n // 2),
-                                  "status": int(status.item())}), flush=True)
 
 
 if __name__ == "__main__":
