@@ -45,6 +45,12 @@ METRIC = "MoE layer tokens/s; decode HBM GB/s & prefill TFLOPS vs B200 roofline"
 
 
 def config_for(name: str, experts: int = 0, tokens: int = 0) -> dict:
+    if name.startswith("okc"):
+        # the reference operator's own shape and contract (H = I = 4096, 32 of 256 experts local, top-8,
+        # precomputed routes, post-norm), at one of its six judged loads (1, 16, 32 decode; 8, 128, 256 verify)
+        T = int(name.split(":")[1]) if ":" in name else 1
+        return dict(workload=f"okc_moe_w4a16_T{T}", E=256, H=4096, I=4096, T=T, k=8, bias_std=0.0, zipf=0.0,
+                    local=32)
     if name.startswith("qwen"):
         T = int(name.split(":")[1]) if ":" in name else 64
         cfg = dict(workload=f"qwen3_30b_a3b_moe_T{T}", E=128, H=2048, I=768, T=T, k=8, bias_std=0.0)
@@ -73,6 +79,7 @@ def parse():
     ap.add_argument("--experts", type=int, default=0, help="override the expert count (small profiling cases)")
     ap.add_argument("--tokens", type=int, default=0, help="override the token count (small profiling cases)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--pdl", type=int, default=0, help="1: decode steps use programmatic dependent launch")
     return ap.parse_args()
 
 
@@ -238,7 +245,7 @@ def run_xcb(a, cfg, rank, world, dist):
         xs.append(x)
         lgs.append(lg)
     outs = [torch.empty((T, H), dtype=torch.bfloat16, device=dev) for _ in range(P)]
-    calls = [layer.build_call(xs[i], lgs[i], k, out=outs[i], return_routing=True) for i in range(P)]
+    calls = [layer.build_call(xs[i], lgs[i], k, out=outs[i], return_routing=True, pdl=bool(a.pdl)) for i in range(P)]
     torch.cuda.synchronize()
     # distinct experts per input (for the algorithmic byte count)
     for c in calls:
@@ -481,7 +488,7 @@ def run_e2e(a, layer, xs, lgs, k, P, dist):
     xd = [torch.empty_like(xs[0]) for _ in range(2)]
     ld = [torch.empty_like(lgs[0]) for _ in range(2)]
     od = [torch.empty((T, H), dtype=torch.bfloat16, device=dev) for _ in range(2)]
-    calls = [layer.build_call(xd[b], ld[b], k, out=od[b]) for b in range(2)]
+    calls = [layer.build_call(xd[b], ld[b], k, out=od[b], pdl=bool(a.pdl)) for b in range(2)]
     comp = torch.cuda.current_stream(dev)
     copy = torch.cuda.Stream(dev)
     up = [torch.cuda.Event() for _ in range(2)]    # inputs of buffer b are on the device
@@ -560,6 +567,7 @@ def finish(a, cfg, world, ms, kern_ms, e2e_ms, u_avg, P, clk, cpu):
                 "fp32 N(0,1) router logits",
         "config": {"workload": cfg["workload"], "tokens": T, "hidden": H, "inter": I, "experts": E, "top_k": k,
                    "router_bias_std": cfg["bias_std"], "parallelism": "replicas" if world > 1 else "single",
+                   "pdl": bool(getattr(a, "pdl", 0)),
                    "l2": f"{P} rotating inputs; 6.3 GB of packed weights resident (>126 MB L2); "
                          f"{u_avg:.1f} distinct experts per step on average"},
         "roofline": roof,
@@ -611,11 +619,140 @@ def run_reference(a, cfg):
     }
 
 
+# ----------------------------------------------------------------------------------------------- reference shape
+def okc_weights(dev, seed: int = 4096):
+    """NVFP4 weights of the 32 local experts at the reference's shape (H = I = 4096), drawn with torch alone so that
+    both arms time the same layer and the reference arm loads nothing of this repository's CUDA library: uniformly
+    random E2M1 codes, E4M3 block scales uniform over the bytes 0x30..0x38 (0.5 .. 1, positive normals as the
+    reference's PRMT-decode build requires), global scales 0.01, post-norm weights bf16 N(0, 0.1)."""
+    import torch
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    E, H, I = 32, 4096, 4096
+    u8 = lambda shape, lo, hi: torch.randint(lo, hi, shape, generator=g, device=dev, dtype=torch.uint8)
+    return {"w13": u8((E, 2 * I, H // 2), 0, 256), "w13_sf": u8((E, 2 * I, H // 16), 0x30, 0x39),
+            "w13_gs": torch.full((E,), 0.01, device=dev), "w2": u8((E, H, I // 2), 0, 256),
+            "w2_sf": u8((E, H, I // 16), 0x30, 0x39), "w2_gs": torch.full((E,), 0.01, device=dev),
+            "post_norm_w": (torch.randn(H, generator=g, device=dev) * 0.1).to(torch.bfloat16)}
+
+
+def okc_batch(T: int, dev, seed: int):
+    """bf16 N(0,1) activations and the top-8 of N(0,1) logits over 256 experts with softmax weights."""
+    import torch
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn((T, 4096), generator=g, device=dev).to(torch.bfloat16)
+    top, ids = torch.topk(torch.randn((T, 256), generator=g, device=dev), 8, dim=1)
+    cfg = {"bs": T, "d_hidden": 4096, "d_expert": 4096, "n_experts": 256, "local_start": 0, "local_count": 32,
+           "top_k": 8, "sharding": "ep8"}
+    return {"hidden_states": x, "topk_ids": ids.to(torch.int32), "topk_weights": torch.softmax(top, dim=1),
+            "config": cfg}
+
+
+def run_okc(a, cfg):
+    """Configuration ``okc:T``: the reference operator's contract at its own shape, on one GPU, L2 flushed (256 MiB
+    read) before every timed step as the reference's paired bench does.  ``--impl xcb`` times this library's
+    ``kernel_fn``; ``--impl reference`` times the reference's own CUDA kernel (built from its sources into
+    oracle/_ref/ by oracle/build_ref.py, driven by oracle/okc_ref.py).  ``e2e`` adds, every step, the host->device
+    copies of x, ids and weights from pinned memory and the device->host copy of the output."""
+    import torch
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    T, H = cfg["T"], cfg["H"]
+    weights = okc_weights(dev)
+    if a.impl == "reference":
+        from oracle import okc_ref
+
+        try:
+            state = okc_ref.prepare(weights)
+            okc_ref.module(okc_ref.build_for(T))
+        except okc_ref.Unavailable as e:
+            return {"impl": "reference", "unavailable": str(e), "config": {"workload": cfg["workload"]}}
+        fn = lambda d: okc_ref.kernel_fn(d, state)
+        launches = (T + okc_ref.CHUNK_TOKENS - 1) // okc_ref.CHUNK_TOKENS
+        what = f"the reference's own CUDA kernel ({okc_ref.build_for(T)} build, oracle/_ref)"
+    else:
+        from xcalibur_b200 import kernel_fn, prepare
+
+        state = prepare(weights, local_start=0, local_count=32, n_experts=256)
+        fn = lambda d: kernel_fn(d, state)
+        launches = 1 if T * 8 <= 256 and T <= 32 else 5
+        what = "xcalibur_b200 kernel_fn"
+    del weights
+    torch.cuda.empty_cache()
+    P = 16
+    batches = [okc_batch(T, dev, seed=100 + i) for i in range(P)]
+    U = [int(torch.unique(b["topk_ids"][b["topk_ids"] < 32]).numel()) for b in batches]
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)   # 256 MiB, twice the L2
+    flush.fill_(1.0)
+    for i in range(max(3, a.warmup)):
+        fn(batches[i % P])
+    torch.cuda.synchronize()
+    K = a.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    for i in range(K):
+        flush.sum()
+        ev[i][0].record()
+        fn(batches[i % P])
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in ev) / K
+    # end to end: pinned host inputs in, output out, every step (after the same flush)
+    host = [{k: (v.cpu().pin_memory() if torch.is_tensor(v) else v) for k, v in b.items()} for b in batches]
+    oh = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    for i in range(K):
+        hb = host[i % P]
+        flush.sum()
+        ev2[i][0].record()
+        d = {k: (v.to(dev, non_blocking=True) if torch.is_tensor(v) else v) for k, v in hb.items()}
+        oh.copy_(fn(d), non_blocking=True)
+        ev2[i][1].record()
+    torch.cuda.synchronize()
+    e2e_ms = sum(e0.elapsed_time(e1) for e0, e1 in ev2) / K
+    u_avg = sum(U[i % P] for i in range(K)) / K
+    from xcalibur_b200 import synth
+
+    hbm, _, _, src = load_peaks()
+    alg = u_avg * synth.layer_bytes(1, H, H) + 2 * T * H * 2 + T * 8 * 8
+    achieved = alg / (ms * 1e-3) / 1e9
+    res = {
+        "metric": METRIC, "value": round(T / (ms * 1e-3), 2), "unit": "tokens/s", "n_gpus": 1, "steps": K,
+        "warmup": max(3, a.warmup), "ms_per_step": round(ms, 5), "us_per_step": round(ms * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "nvfp4 weights (e2m1 + e4m3 block scales) x bf16 activations, fp32 accumulate",
+        "data": "synthetic: random NVFP4 codes and scales, bf16 N(0,1) activations, top-8 of N(0,1) logits",
+        "config": {"workload": cfg["workload"], "tokens": T, "hidden": H, "inter": H, "experts": 256,
+                   "local_experts": 32, "top_k": 8, "contract": "reference kernel_fn: precomputed routes, post-norm",
+                   "implementation": what,
+                   "l2": f"256 MiB read flush before every timed step; {u_avg:.1f} distinct local experts per step"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "peak_source": src, "traffic": None,
+                     "kernel_timing": "CUDA events around each step's launches", "algorithmic_bytes": int(alg)},
+        "e2e": {"value": round(T / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * H * 2 + T * 8 * 8, "d2h_bytes_per_step": T * H * 2},
+        "gpu_launches": K * launches, "clocks": clk,
+    }
+    if a.impl == "reference":
+        res["impl"] = "reference"
+        res["cpu_baseline"] = {"value": res["value"], "unit": "tokens/s", "cores": 0, "kind": "reference",
+                               "device": "GPU", "sample": f"{K} steps of {cfg['workload']} through {what}"}
+    return res
+
+
 def main():
     a = parse()
     cfg = config_for(a.config, a.experts, a.tokens)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if "local" in cfg:                 # the reference's own shape: one GPU, both arms on the GPU
+        if rank == 0:
+            print(json.dumps(run_okc(a, cfg)), flush=True)
+        return
     if a.impl == "reference":
         if rank == 0:
             # reduce the per-step sample so the whole run stays within a few minutes

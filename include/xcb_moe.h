@@ -41,6 +41,10 @@ extern "C" {
 #define XCB_FLAG_POST_NORM 1        /* reference contract: y *= (1 + post_norm_w); out = sum w * y / rms(y) */
 #define XCB_FLAG_DECODE_PATH 2      /* force the decode kernel (default below 257 routes and 33 tokens)       */
 #define XCB_FLAG_PREFILL_PATH 4     /* force the prefill path: tcgen05 grouped GEMMs (default above)         */
+#define XCB_FLAG_PDL 8              /* single-launch decode calls use programmatic dependent launch: the kernel
+                                       may start before the previous kernel of the stream ends and waits
+                                       (griddepcontrol.wait) before its first global read; the reference's
+                                       PDL switch, moe_w4a16.py:169, :2864-2878                                */
 
 /* Shape of one prepared layer.  total_experts is the router width (logits columns, valid topk ids);
  * experts [expert_offset, expert_offset + num_experts) are held in the packed buffers (the reference's
@@ -163,7 +167,9 @@ int xcb_moe_read_status(void* workspace, int32_t* device_status, cudaStream_t st
  * 1 = the same with an L2 evict-first hint, 2 = 16-byte vector loads; ctas_per_sm CTAs of `threads` threads per SM.
  * With `regions` (device int64 byte offsets, `nreg` of them) the CTAs split into nreg groups that each stream one
  * region of bytes/nreg bytes, as the decode kernel streams a few experts.  Time it with events on `stream`;
- * status gets XCB_STATUS_DEVICE_TIMEOUT if a ring wait expired. */
+ * status gets XCB_STATUS_DEVICE_TIMEOUT if a ring wait expired.  Every byte streamed is read: `sink` (4 bytes, zeroed
+ * by the caller) receives the XOR of every 32-bit word read, so a caller can check that the probe streamed what it
+ * claims (each CTA streams (bytes / CTAs) rounded down to a multiple of chunk, 16 for mode 2). */
 int xcb_hbm_probe(const void* src, size_t bytes, int mode, int chunk, int stages, int ctas_per_sm, int threads,
                   const long long* regions, int nreg, int32_t* status, float* sink, cudaStream_t stream);
 

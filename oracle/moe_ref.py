@@ -101,11 +101,11 @@ def moe_forward(x_bf16_bits, ids, weights, w13, w13_sf, w13_gs, w2, w2_sf, w2_gs
         if p0 == p1:
             continue
         xe = torch.from_numpy(np.ascontiguousarray(x[tok[p0:p1]]))
-        wa = torch.from_numpy(nvfp4.dequantize(w13[e], w13_sf[e], w13_gs[e]))
+        wa = torch.from_numpy(nvfp4.dequantize_fast(w13[e], w13_sf[e], w13_gs[e]))
         gu = (xe @ wa.T).numpy()
         g, u = gu[:, :inter], gu[:, inter:]
         h = bf16_round((g / (np.float32(1.0) + np.exp(-g))) * u)
-        wb = torch.from_numpy(nvfp4.dequantize(w2[e], w2_sf[e], w2_gs[e]))
+        wb = torch.from_numpy(nvfp4.dequantize_fast(w2[e], w2_sf[e], w2_gs[e]))
         y = (torch.from_numpy(h) @ wb.T).numpy()
         if gamma is not None:
             y = (y * gamma[None, :]).astype(np.float32)

@@ -10,10 +10,15 @@ Two groups:
     transform at :3903-3933), decoded with the reference's shipped decoder ``_XC_DQ4`` (moe_w4a16.py:3475,
     restated below and checked against the reference's source text) and its e4m3 LUT (moe_w4a16.py:3315-3318),
     giving e2m1(code) * e4m3(scale) for every (row, k).
+* ``ref_okc_pack.json``: digests of the reference's own ``prepare`` repacks (``_pack_codes`` with its GF(2) word
+  transform, ``_pack_scales``, ``_fat_order``, ``_unit_order``, moe_w4a16.py:3168-3209, :3903-3933; the e4m3 LUT,
+  :3313-3318) on seeded codes and scales of one 256-row, K = 4096 expert slice, for the gate_up row order with its
+  sign fold and for the down row order.  They pin ``oracle/okc_ref.py``, which rebuilds the reference's layouts on
+  the GPU box (where the reference's Python is absent) to run its prebuilt kernel.
 * ``layer_c1.json``: checksums of the CPU oracle's layer output on the seeded C1 configuration (guards the
   oracle against drift; no reference needed).
 
-Run:  python tests/golden/make_golden.py --reference /path/to/xCalibur
+Run:  python tests/golden/make_golden.py --reference /path/to/xCalibur  [--okc-only]
 """
 from __future__ import annotations
 
@@ -112,6 +117,50 @@ def make_ref_fixtures(ref_root: str):
     print("wrote ref_gf2.json, ref_dequant.npz")
 
 
+OKC_PACK_SEED = 2024
+
+
+def okc_pack_inputs():
+    """Seeded codes and scale bytes of one 256-row, K = 4096 slice, for gate_up (I = 128) and for down."""
+    rng = np.random.default_rng(OKC_PACK_SEED)
+    c13 = rng.integers(0, 256, (256, 2048), dtype=np.uint8)
+    s13 = rng.integers(0x08, 0x7F, (256, 256), dtype=np.uint8)
+    c2 = rng.integers(0, 256, (256, 2048), dtype=np.uint8)
+    s2 = rng.integers(0x08, 0x7F, (256, 256), dtype=np.uint8)
+    return c13, s13, c2, s2
+
+
+def _sha(a) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def make_okc_pack_fixture(ref_root: str):
+    sys.path.insert(0, os.path.join(ref_root, "kernels", "moe_w4a16_h200"))
+    import torch
+    import moe_w4a16 as m
+
+    c13, s13, c2, s2 = (torch.from_numpy(a) for a in okc_pack_inputs())
+    I = 128
+    rb = torch.arange(I // 8)
+    g = torch.arange(8)
+    rows_a = torch.stack((8 * rb[:, None] + g[None, :], I + 8 * rb[:, None] + g[None, :]), 1).reshape(-1)
+    rows_b = torch.arange(256)
+    out = {}
+    for tag, codes, sf, rows in (("gate_up", c13 ^ 0x88, s13, rows_a), ("down", c2, s2, rows_b)):
+        wds = m._pack_codes(codes, rows)
+        scs = m._pack_scales(sf.view(torch.float8_e4m3fn), rows)
+        out[tag] = {"words": _sha(wds.numpy()), "scales": _sha(scs.numpy()),
+                    "fat": _sha(m._fat_order(wds, scs).numpy()), "unit": _sha(m._unit_order(wds, scs).numpy()),
+                    "words_head": [int(v) for v in wds[:8]]}
+    lut = (torch.arange(256, dtype=torch.int32).to(torch.uint8).view(torch.float8_e4m3fn).float()
+           * 2.0**64).to(torch.bfloat16).view(torch.int16).to(torch.int32) & 0xFFFF
+    out["lut"] = _sha((lut | (lut << 16)).to(torch.int32).numpy())
+    out["seed"] = OKC_PACK_SEED
+    with open(os.path.join(HERE, "ref_okc_pack.json"), "w") as f:
+        json.dump(out, f, indent=1)
+    print("wrote ref_okc_pack.json")
+
+
 def layer_digest(out_bits, ids, wts):
     h = lambda a: hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
     return {"out_sha256": h(out_bits), "ids_sha256": h(ids), "weights_sha256": h(wts)}
@@ -138,9 +187,14 @@ if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=None, help="path of an xCalibur checkout (for the ref_* fixtures)")
     ap.add_argument("--layer-only", action="store_true")
+    ap.add_argument("--okc-only", action="store_true", help="only ref_okc_pack.json")
     a = ap.parse_args()
+    if a.okc_only:
+        make_okc_pack_fixture(a.reference)
+        sys.exit(0)
     if not a.layer_only:
         if not a.reference:
             ap.error("--reference is required for the ref_* fixtures")
         make_ref_fixtures(a.reference)
+        make_okc_pack_fixture(a.reference)
     make_layer_fixture()

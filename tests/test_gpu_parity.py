@@ -352,3 +352,46 @@ def test_bench_reference_arm_experts_match_library(dev):
     host = bench.reference_arm_experts(cfg, used, seed=99, device=dev)
     for name in ("w13", "w13_sf", "w13_gs", "w2", "w2_sf", "w2_gs"):
         assert np.array_equal(host[name], to_np(full[name][torch.as_tensor(used, device=dev)])), name
+
+
+@pytest.mark.parametrize("post_norm", [False, True])
+def test_pdl_chained_launches_match_plain_launches(dev, post_norm):
+    """Programmatic dependent launch (the reference's PDL switch, moe_w4a16.py:169, :2864-2878): a chain of decode
+    calls where each call's input is the previous call's output, launched back to back with PDL, equals the same
+    chain launched in plain stream order, bit for bit; the chain also replays from a CUDA graph."""
+    from xcalibur_b200 import PreparedMoE, synth
+
+    E, H, I, T, k = 16, 1024, 512, 2, 4
+    weights = synth.make_weights(E, H, I, seed=606, device=dev)
+    pn = (torch.randn(H, device=dev) * 0.1).to(torch.bfloat16) if post_norm else None
+    layer = PreparedMoE(*weights.values(), pn)
+    x, _ = synth.make_inputs(T, H, E, seed=607, device=dev)
+    logits = [synth.make_inputs(T, H, E, seed=610 + i, device=dev)[1] for i in range(6)]
+
+    def chain(pdl):
+        h = x
+        outs = []
+        for lg in logits:
+            h = layer.forward(h, lg, k, post_norm=post_norm, pdl=pdl)   # reads the previous kernel's output
+            outs.append(h)
+        return outs
+
+    plain = [o.clone() for o in chain(False)]
+    fast = chain(True)
+    torch.cuda.synchronize()
+    assert layer.check_device_status() == 0
+    for a, b in zip(plain, fast):
+        assert torch.isfinite(a.float()).all() and a.float().abs().max() > 0
+        assert torch.equal(a, b)
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        chain(True)                                        # the stream's workspace exists before capture
+    torch.cuda.current_stream(dev).wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        captured = chain(True)
+    g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(plain, captured):
+        assert torch.equal(a, b)

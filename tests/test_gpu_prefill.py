@@ -184,3 +184,64 @@ def test_chunked_router_bit_exact(dev, T, k, E, ties):
     assert np.array_equal(i32(offs[3], T * k), order)
     assert np.array_equal(i32(offs[4], E), counts)
     assert np.array_equal(i32(offs[5], E + 1), offsets)
+
+
+# ------------------------------------------------------------------------------------------------ full sizes
+def sample_rows(ids: np.ndarray, n: int = 32) -> np.ndarray:
+    """n token rows for an oracle check at full size: tokens on the most- and the least-loaded experts, then
+    tokens chosen greedily to add as few new experts as possible (the oracle dequantises only the experts the
+    sampled rows use)."""
+    T, k = ids.shape
+    counts = np.bincount(ids.reshape(-1), minlength=int(ids.max()) + 1)
+    used = np.nonzero(counts)[0]
+    picks = []
+    for e in (used[np.argmax(counts[used])], used[np.argmin(counts[used])], used[np.argsort(counts[used])[1]]):
+        t = int(np.nonzero((ids == e).any(axis=1))[0][0])
+        if t not in picks:
+            picks.append(t)
+    have = np.zeros(counts.size, dtype=bool)
+    for t in picks:
+        have[ids[t]] = True
+    while len(picks) < n:
+        new = (~have[ids]).sum(axis=1)
+        new[picks] = k + 1
+        t = int(np.argmin(new))
+        picks.append(t)
+        have[ids[t]] = True
+    return np.array(sorted(picks))
+
+
+def _full_size_check(dev, E, H, I, T, k, seed, bias_std):
+    from xcalibur_b200 import PreparedMoE, synth
+
+    weights = synth.make_weights(E, H, I, seed=seed, device=dev)
+    x, logits = synth.make_inputs(T, H, E, seed=seed + 1, device=dev, bias_std=bias_std)
+    layer = PreparedMoE(*weights.values())
+    out, ids, wts = layer.forward(x, logits, k, return_routing=True)      # the path the library picks
+    torch.cuda.synchronize()
+    assert layer.check_device_status() == 0
+    want_ids, want_w = moe_ref.route_topk(to_np(logits), k)
+    assert np.array_equal(to_np(ids), want_ids)                           # every row, bit for bit
+    assert np.array_equal(to_np(wts).view(np.uint32), want_w.view(np.uint32))
+    assert torch.isfinite(out.float()).all()
+    rows = sample_rows(want_ids)
+    sel = torch.as_tensor(rows, device=dev)
+    want = oracle_layer(x.index_select(0, sel), weights, want_ids[rows], want_w[rows])
+    assert_close_bf16(out.index_select(0, sel), want)
+    return want_ids, rows
+
+
+def test_prefill_deepseek_v3_t4096_sampled_rows(dev):
+    """Configuration 3 at its full size (T = 4096, DeepSeek-V3 shape, router bias N(0, 0.5)): ids and weights of
+    all 32768 routes bit-exact, and 32 rows (on the hottest and the coldest experts, and rows sharing experts)
+    against the oracle."""
+    ids, rows = _full_size_check(dev, 256, 7168, 2048, 4096, 8, 300, 0.5)
+    counts = np.bincount(ids.reshape(-1), minlength=256)
+    hit = np.unique(ids[rows])
+    assert counts.argmax() in hit and counts[counts > 0].min() in counts[hit]
+
+
+@pytest.mark.parametrize("T", [2048, 8192])
+def test_qwen3_large_batches_sampled_rows(dev, T):
+    """Configuration 4 at T = 2048 and 8192 (Qwen3-30B-A3B shape, H=2048, I=768, 128 experts, top-8)."""
+    _full_size_check(dev, 128, 2048, 768, T, 8, 500 + T, 0.0)

@@ -109,3 +109,14 @@ def test_nonlocal_routes_contribute_nothing():
     for t in range(T):
         if not any(4 <= e < 8 for e in ids[t]):
             assert not moe_ref.bf16_bits_to_f32(out[t]).any()
+
+
+def test_fast_dequantize_is_identical():
+    rng = np.random.default_rng(5)
+    c = rng.integers(0, 256, (64, 512), dtype=np.uint8)
+    s = rng.integers(0, 256, (64, 64), dtype=np.uint8)
+    s[(s & 0x7F) == 0x7F] = 0x38                          # no NaN scale bytes
+    for gs in (np.float32(0.0123), np.float32(3.0)):
+        a = nvfp4.dequantize(c, s, gs)
+        b = nvfp4.dequantize_fast(c, s, gs)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))

@@ -120,7 +120,8 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   if (have_logits == have_ids) return XCB_ERR_INVALID_ARG;
   const bool post_norm = (a->flags & XCB_FLAG_POST_NORM) != 0;
   if (post_norm && !w->post_norm_w) return XCB_ERR_INVALID_ARG;
-  if (a->flags & ~(XCB_FLAG_POST_NORM | XCB_FLAG_DECODE_PATH | XCB_FLAG_PREFILL_PATH)) return XCB_ERR_INVALID_ARG;
+  if (a->flags & ~(XCB_FLAG_POST_NORM | XCB_FLAG_DECODE_PATH | XCB_FLAG_PREFILL_PATH | XCB_FLAG_PDL))
+    return XCB_ERR_INVALID_ARG;
   if ((a->flags & XCB_FLAG_DECODE_PATH) && (a->flags & XCB_FLAG_PREFILL_PATH)) return XCB_ERR_INVALID_ARG;
   if (!aligned16(a->hidden_states) || !aligned16(a->out) || !aligned16(w->gate_up) || !aligned16(w->down) ||
       !aligned16(ws))
@@ -207,6 +208,9 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   }
   sp->post_norm = post_norm ? 1 : 0;
   sp->grid_combine = (post_norm || !small) ? 1 : 0;
+  // programmatic dependent launch for the single-launch decode step (a step that runs the router first keeps
+  // plain stream order: its router kernel is what the experts kernel waits for)
+  sp->pdl = (a->flags & XCB_FLAG_PDL) && small ? 1 : 0;
   sp->timeout_ns = timeout_ns;
 
   WidePathParams* wp = &plan->wp;

@@ -19,6 +19,13 @@ __device__ __forceinline__ uint64_t gtimer() {
 // Record an error bit in the workspace status word (read back by xcb_moe_read_status).
 __device__ __forceinline__ void set_status(int* status, int bit) { atomicOr(status, bit); }
 
+// Programmatic dependent launch: a kernel launched with the programmatic-serialisation attribute may start while
+// the previous kernel of its stream is still running; it must wait for that kernel (and its memory) before it
+// reads anything another kernel wrote.  launch_dependents lets the next kernel be scheduled early.  Both are no-ops
+// for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ int ld_acquire(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -63,6 +63,7 @@ struct SkinnyParams {
   int job_tokens;         // most tokens one job holds (sizes the activation staging; the in-kernel router's job split)
   int post_norm;
   int grid_combine;       // 1: grid barrier + distributed combine; 0: per-row-block combine by the CTA completing it
+  int pdl;                // launched with programmatic dependent launch (griddepcontrol.wait before any read)
   unsigned long long timeout_ns;
 };
 

@@ -34,8 +34,9 @@ __global__ void __launch_bounds__(1024) probe_kernel(ProbeParams p) {
     base = p.src + p.regions[r] + per * (blockIdx.x - c0);
   }
   const int tid = threadIdx.x;
+  uint32_t* sum = reinterpret_cast<uint32_t*>(p.sink);
   if (p.mode == 2) {
-    float acc = 0.f;
+    uint32_t acc = 0;
     const uint4* v = reinterpret_cast<const uint4*>(base);
     const size_t n = per / 16;
     const int U = 8;
@@ -47,9 +48,10 @@ __global__ void __launch_bounds__(1024) probe_kernel(ProbeParams p) {
         r[u] = j < n ? __ldcs(v + j) : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
-      for (int u = 0; u < U; ++u) acc += __uint_as_float(r[u].x ^ r[u].y ^ r[u].z ^ r[u].w);
+      for (int u = 0; u < U; ++u) acc ^= r[u].x ^ r[u].y ^ r[u].z ^ r[u].w;
     }
-    if (acc == 1.2345f) p.sink[0] = acc;
+    acc = __reduce_xor_sync(0xffffffffu, acc);
+    if ((tid & 31) == 0) atomicXor(sum, acc);
     return;
   }
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)p.stages * p.chunk);
@@ -81,15 +83,22 @@ __global__ void __launch_bounds__(1024) probe_kernel(ProbeParams p) {
         mbar_wait(full + (i % p.stages), (i / p.stages) & 1, p.timeout_ns, p.status);
     }
   } else {
-    float acc = 0.f;
+    // the consumer warps read every word of every stage (a streaming reduction, as a GEMV reads its weights)
+    uint32_t acc = 0;
+    const int words = p.chunk / 16;
     for (int it = 0; it < nch; ++it) {
       const int st = it % p.stages;
       mbar_wait(full + st, (it / p.stages) & 1, p.timeout_ns, p.status);
-      acc += __uint_as_float(reinterpret_cast<const uint32_t*>(smem + (size_t)st * p.chunk)[(lane + 32 * warp) % (p.chunk / 4)]);
+      const uint4* w = reinterpret_cast<const uint4*>(smem + (size_t)st * p.chunk);
+      for (int i = lane + 32 * warp; i < words; i += 32 * nconsumer_warps) {
+        const uint4 v = w[i];
+        acc ^= v.x ^ v.y ^ v.z ^ v.w;
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty + st);
     }
-    if (acc == 1.2345f) p.sink[0] = acc;
+    acc = __reduce_xor_sync(0xffffffffu, acc);
+    if (lane == 0) atomicXor(sum, acc);
   }
 }
 

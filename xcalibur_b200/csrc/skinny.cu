@@ -549,6 +549,13 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
   // uses that token's row, staged before routing into row 0 of buffers 0 and 1
   const bool xpre = p.T == 1 && p.job_tokens == 1;
 
+  // with programmatic dependent launch this CTA may be resident before the previous kernel of the stream is done:
+  // every global read below (inputs, workspace) comes after the wait; the next kernel may be scheduled from now on
+  // (it waits for this whole grid before it reads anything)
+  if (p.pdl) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_launch_dependents();
+  }
   // one token with logits: warp 0 loads the row now, so the load overlaps the set-up below
   const bool route_one = p.small_route && p.T == 1 && p.logits != nullptr;
   uint32_t key[16];
@@ -1055,8 +1062,21 @@ int launch_skinny(const SkinnyParams& p, cudaStream_t stream) {
   SkLayout plan;
   int rc = skinny_config(&grid, &plan, p.H, p.I, p.job_tokens, p.small_route ? p.T * p.k : 0);
   if (rc != XCB_OK) return rc;
-  skinny_kernel<<<grid, SK_THREADS, plan.total, stream>>>(p, plan);
-  return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
+  if (!p.pdl) {
+    skinny_kernel<<<grid, SK_THREADS, plan.total, stream>>>(p, plan);
+    return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(SK_THREADS);
+  cfg.dynamicSmemBytes = (size_t)plan.total;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, skinny_kernel, p, plan) == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
 }
 
 }  // namespace xcb
