@@ -46,7 +46,7 @@ def oracle_layer(x, weights: dict, ids: np.ndarray, wts: np.ndarray, *, post_nor
     return out
 
 
-def assert_close_bf16(got: torch.Tensor, want_bits: np.ndarray, rtol=RTOL, atol=ATOL):
+def assert_close_bf16(got: torch.Tensor, want_bits: np.ndarray, rtol=RTOL, atol=ATOL, frobenius=5e-3):
     g = moe_ref.bf16_bits_to_f32(bf16_bits(got))
     w = moe_ref.bf16_bits_to_f32(want_bits)
     assert np.isfinite(g).all()
@@ -55,4 +55,6 @@ def assert_close_bf16(got: torch.Tensor, want_bits: np.ndarray, rtol=RTOL, atol=
     assert not bad.any(), f"{bad.sum()} of {bad.size} outside tolerance; max err {err.max():.3g}"
     # and in aggregate the kernel tracks the reference much more tightly than the per-element bound
     rel = np.linalg.norm(g - w) / max(np.linalg.norm(w), 1e-30)
-    assert rel < 5e-3, f"relative Frobenius error {rel:.3g}"
+    if frobenius is not None:
+        assert rel < frobenius, f"relative Frobenius error {rel:.3g}"
+    return rel

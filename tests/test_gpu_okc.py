@@ -4,9 +4,12 @@ The reference operator is shape-locked (H = I = 4096, 256 experts of which 32 ar
 kernels/moe_w4a16_h200/moe_w4a16.py:105-110) and was judged at six loads: 1, 16 and 32 decode tokens and 8, 128
 and 256 verify tokens (kernels/moe_w4a16_h200/README.md:86-95).  Its kernel, built from its own sources by
 ``oracle/build_ref.py`` and driven through ``oracle/okc_ref.py``, runs beside this library's ``kernel_fn`` on the
-same seeded weights and routes; the outputs must agree within the north_star tolerance (rtol / atol 1e-2), and at
-one load both are also checked against the CPU oracle.  If the reference's kernel was not built, or the reference's
-own admission check finds that one CTA per SM does not fit, the test is skipped with that reason."""
+same seeded weights and routes.  At every load both outputs are checked against the CPU oracle within the
+north_star tolerance (rtol / atol 1e-2 per element), and against each other; this library's output must also track
+the oracle in aggregate (relative Frobenius error < 5e-3).  The reference's M = 1 build accumulates in bf16
+within 16-value groups (moe_w4a16.py:3486, its grouped-HFMA2 program), so the aggregate bound is not applied to
+it.  If the reference's kernel was not built, or the reference's own admission check finds that one CTA per SM does
+not fit, the test is skipped with that reason."""
 import pytest
 import torch
 
@@ -72,24 +75,11 @@ def test_layer_matches_reference_kernel_at_okc_loads(okc, cuda_device, T):
     want = okc_ref.kernel_fn(data, ref)
     torch.cuda.synchronize(cuda_device)
     assert ours["layer"].check_device_status() == 0
-    assert_close_bf16(got, bf16_bits(want))
-    # tokens without a local route are exactly zero in both
-    none_local = ~((ids >= 0) & (ids < 32)).any(dim=1)
-    assert not got[none_local].float().any() and not want[none_local].float().any()
-
-
-def test_reference_kernel_and_layer_match_the_oracle(okc, cuda_device):
-    """At the 8-token load, both the reference's kernel and this library's layer against the CPU oracle."""
-    from oracle import okc_ref
-    from xcalibur_b200 import kernel_fn
-
-    weights, ours, ref = okc
-    x, ids, wts = okc_inputs(8, cuda_device, seed=18)
-    data = okc_data(x, ids, wts)
-    got = kernel_fn(data, ours)
-    want = okc_ref.kernel_fn(data, ref)
-    torch.cuda.synchronize(cuda_device)
     exp = oracle_layer(x, weights, ids.cpu().numpy(), wts.cpu().numpy(), post_norm_w=weights["post_norm_w"],
                        local_start=0, local_count=32)
     assert_close_bf16(got, exp)
-    assert_close_bf16(want, exp)
+    assert_close_bf16(want, exp, frobenius=None)
+    assert_close_bf16(got, bf16_bits(want), frobenius=None)
+    # tokens without a local route are exactly zero in both
+    none_local = ~((ids >= 0) & (ids < 32)).any(dim=1)
+    assert not got[none_local].float().any() and not want[none_local].float().any()

@@ -358,7 +358,9 @@ def test_bench_reference_arm_experts_match_library(dev):
 def test_pdl_chained_launches_match_plain_launches(dev, post_norm):
     """Programmatic dependent launch (the reference's PDL switch, moe_w4a16.py:169, :2864-2878): a chain of decode
     calls where each call's input is the previous call's output, launched back to back with PDL, equals the same
-    chain launched in plain stream order, bit for bit; the chain also replays from a CUDA graph."""
+    chain launched in plain stream order (bit for bit without the post-norm; with it the per-route sums of squares
+    are fp32 atomics, so within the tolerance); the chain also replays from a CUDA graph.  Without the post-norm
+    the magnitudes shrink quadratically along the chain, so that chain is three calls long."""
     from xcalibur_b200 import PreparedMoE, synth
 
     E, H, I, T, k = 16, 1024, 512, 2, 4
@@ -366,7 +368,12 @@ def test_pdl_chained_launches_match_plain_launches(dev, post_norm):
     pn = (torch.randn(H, device=dev) * 0.1).to(torch.bfloat16) if post_norm else None
     layer = PreparedMoE(*weights.values(), pn)
     x, _ = synth.make_inputs(T, H, E, seed=607, device=dev)
-    logits = [synth.make_inputs(T, H, E, seed=610 + i, device=dev)[1] for i in range(6)]
+    logits = [synth.make_inputs(T, H, E, seed=610 + i, device=dev)[1] for i in range(6 if post_norm else 3)]
+
+    def same(a, b):
+        if post_norm:
+            return torch.allclose(a.float(), b.float(), rtol=1e-2, atol=1e-2)
+        return torch.equal(a, b)
 
     def chain(pdl):
         h = x
@@ -382,7 +389,7 @@ def test_pdl_chained_launches_match_plain_launches(dev, post_norm):
     assert layer.check_device_status() == 0
     for a, b in zip(plain, fast):
         assert torch.isfinite(a.float()).all() and a.float().abs().max() > 0
-        assert torch.equal(a, b)
+        assert same(a, b)
     s = torch.cuda.Stream(dev)
     s.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(s):
@@ -394,4 +401,4 @@ def test_pdl_chained_launches_match_plain_launches(dev, post_norm):
     g.replay()
     torch.cuda.synchronize()
     for a, b in zip(plain, captured):
-        assert torch.equal(a, b)
+        assert same(a, b)

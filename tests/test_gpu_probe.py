@@ -20,7 +20,10 @@ def test_probe_reads_every_byte(cuda_device, mode, chunk, stages, ctas):
     G = sms * ctas
     per = 16 * 32768                                     # bytes per CTA: a multiple of every chunk above
     g = torch.Generator(device=cuda_device).manual_seed(mode)
-    buf = torch.randint(-2**31, 2**31 - 1, (G * per // 4,), generator=g, device=cuda_device, dtype=torch.int32)
+    raw = torch.randint(-2**31, 2**31 - 1, (G * per // 4 + 256,), generator=g, device=cuda_device,
+                        dtype=torch.int32)
+    skip = ((-raw.data_ptr()) % 1024) // 4                 # the probe wants a 1 KB aligned source
+    buf = raw[skip:skip + G * per // 4]
     status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
     sink = torch.zeros(1, dtype=torch.float32, device=cuda_device)
     stream = torch.cuda.current_stream(cuda_device).cuda_stream
