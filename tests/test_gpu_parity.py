@@ -402,3 +402,25 @@ def test_pdl_chained_launches_match_plain_launches(dev, post_norm):
     torch.cuda.synchronize()
     for a, b in zip(plain, captured):
         assert same(a, b)
+
+
+@pytest.mark.parametrize("scale", [1e-7, 1e-3, 3e4])
+def test_decode_keeps_relative_precision_at_any_activation_scale(dev, scale):
+    """The decode kernel converts activations to f16 with a per-token power-of-two scale; rows whose largest
+    magnitude is far below or above 1 must keep their relative precision (a row of 1e-7 values would otherwise sink
+    into f16's subnormal range and a row of 3e4 values overflow it)."""
+    from xcalibur_b200 import PreparedMoE
+
+    rng = np.random.default_rng(71)
+    E, H, I, T, k = 8, 1024, 512, 3, 2
+    w = moe_ref.make_weights(rng, E, H, I)
+    x = moe_ref.f32_to_bf16_bits(rng.standard_normal((T, H), dtype=np.float32) * np.float32(scale))
+    logits = rng.standard_normal((T, E), dtype=np.float32)
+    layer = PreparedMoE(*_weights_from_np(w, dev).values())
+    xd = torch.from_numpy(x.view(np.int16)).to(dev).view(torch.bfloat16)
+    out = layer.forward(xd, torch.from_numpy(logits).to(dev), k, path="decode")
+    torch.cuda.synchronize()
+    want, _, _ = moe_ref.moe_layer(x, logits, *w, k)
+    wf = moe_ref.bf16_bits_to_f32(want)
+    assert np.abs(wf).max() > 0
+    assert_close_bf16(out, want, atol=1e-2 * float(np.abs(wf).max()))

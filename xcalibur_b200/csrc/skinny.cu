@@ -8,8 +8,8 @@
 //   E4M3 by cvt.rn.f16x2.e4m3x2), and four m16n8k16 f16 tensor-core steps fed from registers.  Every product
 //   e2m1 * e4m3 has at most 6 significant bits and lies in [2^-10, 2688], so the f16 weight is exact.  The
 //   activations are converted to f16 once per segment in shared memory, each token scaled by a power of two
-//   2^-e chosen from its largest magnitude so that it cannot overflow f16 (e = 0 for |x| < 2^15); the epilogue
-//   multiplies the fp32 sums back by 2^e.  At T <= 8 tokens per expert the weights are used once, and a
+//   2^-e that puts its largest magnitude in [2^14, 2^15), so it neither overflows f16 nor sinks into f16's
+//   subnormal range; the epilogue multiplies the fp32 sums back by 2^e.  At T <= 8 tokens per expert the weights are used once, and a
 //   register-fed MMA reads no shared memory for them.
 // * Weight stream: warp 16 copies packed weights into a ring of 3-8 stages with 1-D bulk copies (TMA engine,
 //   L2 evict-first).  A stage holds PER consecutive slices for each of the 16 compute warps, PER chosen per
@@ -465,7 +465,8 @@ __device__ void sk_route_one(const SkinnyParams& p, const uint32_t (&key)[16], S
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // Convert `ntok` staged bf16 rows of K values to f16 in place (one warp), each row scaled by 2^-e with e chosen
-// from its largest magnitude so that the result cannot overflow f16; e is returned per row in xexp.
+// from its largest magnitude so that the result neither overflows f16 nor loses bits in its subnormal range; e is
+// returned per row in xexp.
 __device__ void sk_rows_to_f16(uint8_t* buf, int pitch, int ntok, int K, int* xexp) {
   const int lane = threadIdx.x & 31, nv = K / 8;
   for (int n = 0; n < ntok; ++n) {
@@ -479,7 +480,9 @@ __device__ void sk_rows_to_f16(uint8_t* buf, int pitch, int ntok, int K, int* xe
     }
     m = __reduce_max_sync(0xffffffffu, m);
     const int E = (int)(m >> 7);           // bf16 exponent field of the largest magnitude: |x| < 2^(E - 126)
-    const int e = E > 141 ? E - 141 : 0;   // scaled magnitudes stay below 2^15
+    // the row's largest magnitude lands in [2^14, 2^15): a large row cannot overflow f16 and a small one does not
+    // sink into its subnormal range (e = -126 at most, so 2^e and 2^-e stay normal fp32 numbers)
+    const int e = max(E - 141, -126);
     const float sc = __uint_as_float((uint32_t)(127 - e) << 23);
     for (int v = lane; v < nv; v += 32) {
       const uint4 q = row[v];
@@ -517,7 +520,7 @@ __device__ int sk_row_to_f16_warps(uint8_t* row, uint8_t* copy, int K, int* part
   int mm = 0;
   for (int i = 0; i < nw; ++i) mm = max(mm, part[i]);
   const int E = mm >> 7;
-  const int e = E > 141 ? E - 141 : 0;
+  const int e = max(E - 141, -126);  // as in sk_rows_to_f16
   const float sc = __uint_as_float((uint32_t)(127 - e) << 23);
   for (int v = v0 + lane; v < v1; v += 32) {
     const uint4 q = r[v];
