@@ -41,21 +41,28 @@
 
 namespace xcb {
 
-// Optional timeline trace (builds with -DXCB_TRACE=1 only): %globaltimer stamps, clock64 spans and counters per
-// CTA, read back with xcb_trace_read.  Off in the shipped library.
+// Optional timeline trace, read back with xcb_trace_read (off in the shipped library): -DXCB_TRACE=1 records
+// %globaltimer stamps, clock64 spans and counters per CTA; -DXCB_TRACE=2 only each CTA's start and exit times and
+// its SM (light enough not to change the timing).
 #ifndef XCB_TRACE
 #define XCB_TRACE 0
 #endif
 #if XCB_TRACE
 constexpr int kTraceSlots = 32;
 __device__ unsigned long long g_trace[1024 * kTraceSlots];
+#define TRACE_EDGE(slot) (g_trace[blockIdx.x * kTraceSlots + (slot)] = gtimer())
+#endif
+#if XCB_TRACE == 1
 #define TRACE_AT(slot) (g_trace[blockIdx.x * kTraceSlots + (slot)] = gtimer())
 #define TRACE_ADD(slot, v) atomicAdd(&g_trace[blockIdx.x * kTraceSlots + (slot)], (unsigned long long)(v))
 #define TRACE_GET(slot) (*(volatile unsigned long long*)&g_trace[blockIdx.x * kTraceSlots + (slot)])
 #define TRACE_T0(name) const unsigned long long name = clock64()
 #define TRACE_SPAN(slot, name) TRACE_ADD(slot, clock64() - (name))
-#define TRACE_ONCE(slot) (TRACE_GET(slot) == 0ull ? (void)TRACE_AT(slot) : (void)0)
+#define TRACE_ONCE(slot) ((trace_once & (1u << (slot))) ? (void)0 : (void)(trace_once |= 1u << (slot), TRACE_AT(slot)))
 #else
+#ifndef TRACE_EDGE
+#define TRACE_EDGE(slot) ((void)0)
+#endif
 #define TRACE_AT(slot) ((void)0)
 #define TRACE_ADD(slot, v) ((void)0)
 #define TRACE_T0(name) ((void)0)
@@ -63,6 +70,9 @@ __device__ unsigned long long g_trace[1024 * kTraceSlots];
 #define TRACE_ONCE(slot) ((void)0)
 #endif
 
+#ifndef XCB_SK_MUL
+#define XCB_SK_MUL 41  // share permutation multiplier (prime)
+#endif
 constexpr int SK_NW = 16;                               // compute warps
 constexpr int SK_W_PROD = SK_NW;                        // weight producer warp
 constexpr int SK_W_ACT = SK_NW + 1;                     // activation staging warp
@@ -118,7 +128,7 @@ struct SkSegments {
       // the share a CTA takes differs per sequence (a bijection of the CTA index: 41 is prime, so coprime with G
       // unless G is a multiple of it): a CTA whose share of one sequence streams slowly (the slow part of the
       // address space) gets other parts of the others, which evens the CTAs' finish times (measured 1.5 %)
-      const int mul = G % 41 ? 41 : 1;
+      const int mul = G % XCB_SK_MUL ? XCB_SK_MUL : 1;
       const int sb = (int)(((long long)bid * mul + q * 17) % G);
       a[q] = (long long)j0 * nrb + cnt * sb / G;
       b[q] = (long long)j0 * nrb + cnt * (sb + 1) / G;
@@ -550,7 +560,10 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
   const int G = gridDim.x, bid = blockIdx.x;
   // one token and one row per job (so not an expert named twice by precomputed routing): every phase-A segment
   // uses that token's row, staged before routing into row 0 of buffers 0 and 1
-  const bool xpre = p.T == 1 && p.job_tokens == 1;
+  const bool xpre = p.T == 1;
+#if XCB_TRACE == 1
+  unsigned trace_once = 0;  // TRACE_ONCE slots this thread has stamped
+#endif
 
   // with programmatic dependent launch this CTA may be resident before the previous kernel of the stream is done:
   // every global read below (inputs, workspace) comes after the wait; the next kernel may be scheduled from now on
@@ -564,7 +577,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
   uint32_t key[16];
   if (route_one && warp == 0) warp_topk_load(p.logits, p.E_tot, key);
   if (tid == 0) {
-    TRACE_AT(0);
+    TRACE_EDGE(0);
 #if XCB_TRACE
     {
       uint32_t smid;
@@ -871,10 +884,13 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
         TRACE_SPAN(12, t_x);
         if (ph == 1) TRACE_ONCE(10);
       }
-      const uint8_t* xrow = bufs + (size_t)b * L.rows * L.pitch + (size_t)(g < ntok ? g : 0) * L.pitch;
+      // one token: every route of a job (an expert named twice by precomputed routing gives a job two routes) is
+      // that token, whose row is row 0 (staged once at kernel start for phase A)
+      const bool one = p.T == 1;
+      const uint8_t* xrow = bufs + (size_t)b * L.rows * L.pitch + (size_t)(g < ntok && !one ? g : 0) * L.pitch;
       // column scales 2^e of this lane's tokens 2t, 2t + 1 (rows past the job's tokens are discarded)
-      const float sc0 = __uint_as_float((uint32_t)(127 + cb.xexp[b][min(2 * t, ntok - 1)]) << 23);
-      const float sc1 = __uint_as_float((uint32_t)(127 + cb.xexp[b][min(2 * t + 1, ntok - 1)]) << 23);
+      const float sc0 = __uint_as_float((uint32_t)(127 + cb.xexp[b][one ? 0 : min(2 * t, ntok - 1)]) << 23);
+      const float sc1 = __uint_as_float((uint32_t)(127 + cb.xexp[b][one ? 0 : min(2 * t + 1, ntok - 1)]) << 23);
       for (int i = 0; i < nst; ++i) {
         TRACE_T0(t_f);
         mbar_wait(cb.full + st, sphase, p.timeout_ns, status);
@@ -1002,7 +1018,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
   // -------------------------------------------------------------------- exit: the last CTA resets the counters
   __syncthreads();
   if (tid == 0) {
-    TRACE_AT(8);
+    TRACE_EDGE(8);
     __threadfence();
     const int done = atomicAdd(p.ctl + kCtlExit, 1);
     if (done == G - 1) {
