@@ -37,9 +37,11 @@ if ROOT not in sys.path:
 CONFIGS = {
     "decode": dict(workload="deepseek_v3_moe_decode", E=256, H=7168, I=2048, T=1, k=8, bias_std=0.0),
     "prefill": dict(workload="deepseek_v3_moe_prefill", E=256, H=7168, I=2048, T=4096, k=8, bias_std=0.5),
-    # configuration 5: 16384 tokens per GPU, Zipf(s=1.1) router bias toward low expert ids (the worst case for
-    # contiguous expert shards: bias_e = -1.1 ln(e + 1))
-    "ep": dict(workload="deepseek_v3_moe_ep", E=256, H=7168, I=2048, T=16384, k=8, bias_std=0.0, zipf=1.1),
+    # configuration 5: 16384 tokens per GPU, Zipf(s=1.1) router bias bias_e = -1.1 ln(r_e + 1) where r_e is expert
+    # e's place in a seeded random order (seed 77), so the hot experts fall on different ranks of the contiguous
+    # expert shards (with r_e = e, every hot expert would sit on rank 0)
+    "ep": dict(workload="deepseek_v3_moe_ep", E=256, H=7168, I=2048, T=16384, k=8, bias_std=0.0, zipf=1.1,
+               zipf_order_seed=77),
 }
 METRIC = "MoE layer tokens/s; decode HBM GB/s & prefill TFLOPS vs B200 roofline"
 
@@ -72,7 +74,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="xcb", choices=["xcb", "reference"])
-    ap.add_argument("--config", default="decode")
+    ap.add_argument("--config", default=None,
+                    help="decode (1 GPU default), prefill, qwen:T, ep, okc:T; with several GPUs the default prints "
+                         "the ep line (configuration 5), then the expert-parallel decode line")
     ap.add_argument("--pool", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-tokens", type=int, default=1)
@@ -231,7 +235,8 @@ def run_xcb(a, cfg, rank, world, dist):
     layer = PreparedMoE(*weights.values())
     cpu = None
     if rank == 0 and not a.no_cpu_baseline:
-        x0, l0 = synth.make_inputs(T, H, E, seed=1, device=dev, bias_std=cfg["bias_std"], zipf_s=cfg["zipf"])
+        x0, l0 = synth.make_inputs(T, H, E, seed=1, device=dev, bias_std=cfg["bias_std"], zipf_s=cfg["zipf"],
+                                   zipf_order_seed=cfg.get("zipf_order_seed"))
         n0 = min(T, a.cpu_sample_tokens)
         ids0, wts0, used0 = sample_routes(l0, k, n0)
         cpu = cpu_oracle_sample(host_experts(weights, used0), used0, x0, ids0, wts0, n0)
@@ -241,7 +246,7 @@ def run_xcb(a, cfg, rank, world, dist):
     xs, lgs = [], []
     for i in range(P):
         x, lg = synth.make_inputs(T, H, E, seed=1000 * rank + i + 1, device=dev, bias_std=cfg["bias_std"],
-                                  zipf_s=cfg["zipf"])
+                                  zipf_s=cfg["zipf"], zipf_order_seed=cfg.get("zipf_order_seed"))
         xs.append(x)
         lgs.append(lg)
     outs = [torch.empty((T, H), dtype=torch.bfloat16, device=dev) for _ in range(P)]
@@ -320,7 +325,26 @@ def run_xcb(a, cfg, rank, world, dist):
     return res
 
 
-def run_xcb_ep(a, cfg, rank, world, dist):
+def make_ep_layer(cfg, rank, world):
+    """This rank's shard of the seeded DeepSeek-V3-shaped layer, as an expert-parallel layer (collective)."""
+    import torch
+
+    from xcalibur_b200 import synth
+    from xcalibur_b200.ep import ExpertParallelMoE
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    E, H, I = cfg["E"], cfg["H"], cfg["I"]
+    epr = E // world
+    weights = synth.make_weights(E, H, I, seed=1234, device=dev)      # same layer on every rank; keep this shard
+    shard = {n: t[rank * epr:(rank + 1) * epr].contiguous() for n, t in weights.items()}
+    del weights
+    torch.cuda.empty_cache()
+    layer = ExpertParallelMoE(*shard.values(), total_experts=E)
+    del shard
+    return layer
+
+
+def run_xcb_ep(a, cfg, rank, world, dist, layer):
     """N > 1: expert parallelism.  Every rank holds E / N experts and its own T tokens (weak scaling); a step is one
     layer over every rank's tokens: router, dispatch (NCCL all-to-all over NVLink), the local experts, return and
     combine.  Timed with CUDA events, max over ranks."""
@@ -334,17 +358,11 @@ def run_xcb_ep(a, cfg, rank, world, dist):
     dev = torch.device("cuda", local)
     E, H, I, T, k = cfg["E"], cfg["H"], cfg["I"], cfg["T"], cfg["k"]
     epr = E // world
-    weights = synth.make_weights(E, H, I, seed=1234, device=dev)      # same layer on every rank; keep this shard
-    shard = {n: t[rank * epr:(rank + 1) * epr].contiguous() for n, t in weights.items()}
-    del weights
-    torch.cuda.empty_cache()
-    layer = ExpertParallelMoE(*shard.values(), total_experts=E)
-    del shard
     P = max(1, a.pool if T <= 64 else 2)
     xs, lgs = [], []
     for i in range(P):
         x, lg = synth.make_inputs(T, H, E, seed=1000 * rank + i + 1, device=dev, bias_std=cfg["bias_std"],
-                                  zipf_s=cfg["zipf"])
+                                  zipf_s=cfg["zipf"], zipf_order_seed=cfg.get("zipf_order_seed"))
         xs.append(x)
         lgs.append(lg)
     for i in range(max(3, a.warmup)):
@@ -435,7 +453,6 @@ def run_xcb_ep(a, cfg, rank, world, dist):
         torch.cuda.synchronize()
     dense_p2p = T <= ExpertParallelMoE.DENSE_MAX_TOKENS and layer.p2p is not None
     p2p_error = layer.p2p_error
-    layer.close()  # the peer exchange's buffers (collective)
     u_avg = sum(U[i % P] for i in range(K)) / K
     r_avg = sum(R[i % P] for i in range(K)) / K
     res = finish(a, cfg, world, ms, ms, e2e_ms, u_avg, P, clk, None)
@@ -451,6 +468,9 @@ def run_xcb_ep(a, cfg, rank, world, dist):
     res["roofline"]["kernel"] = "whole expert-parallel step per rank (router, dispatch, local experts, combine)"
     res["roofline"]["step_ms"] = round(ms, 5)
     res["config"]["parallelism"] = f"ep{world}"
+    if cfg.get("zipf"):
+        res["config"]["router_bias"] = (f"zipf(s={cfg['zipf']}): bias_e = -s ln(r_e + 1), r_e = place of expert e in a "
+                                        f"seeded random order (seed {cfg.get('zipf_order_seed')})")
     res["config"]["step_launch"] = "one CUDA graph replay per step" if T <= 32 else "eager (planned exchange)"
     res["config"]["exchange"] = ("NVLink peer memory (dispatch/combine kernels)" if dense_p2p else
                                  "NCCL all-to-all" if T <= 32 else "NCCL all-to-all (planned, uneven splits)")
@@ -597,7 +617,8 @@ def run_reference(a, cfg):
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     E, H, I, T, k = cfg["E"], cfg["H"], cfg["I"], cfg["T"], cfg["k"]
-    x, lg = synth.make_inputs(T, H, E, seed=1, device=dev, bias_std=cfg["bias_std"], zipf_s=cfg["zipf"])
+    x, lg = synth.make_inputs(T, H, E, seed=1, device=dev, bias_std=cfg["bias_std"], zipf_s=cfg["zipf"],
+                              zipf_order_seed=cfg.get("zipf_order_seed"))
     n = min(T, a.cpu_sample_tokens)
     ids, wts, used = sample_routes(lg, k, n)
     host = reference_arm_experts(cfg, used, seed=1234, device=dev)
@@ -746,9 +767,10 @@ def run_okc(a, cfg):
 
 def main():
     a = parse()
-    cfg = config_for(a.config, a.experts, a.tokens)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    names = [a.config] if a.config else (["decode"] if world == 1 else ["ep", "decode"])
+    cfg = config_for(names[0], a.experts, a.tokens)
     if "local" in cfg:                 # the reference's own shape: one GPU, both arms on the GPU
         if rank == 0:
             print(json.dumps(run_okc(a, cfg)), flush=True)
@@ -770,11 +792,21 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         dist = td
+    layer = None
     try:
-        res = run_xcb_ep(a, cfg, rank, world, dist) if world > 1 else run_xcb(a, cfg, rank, world, dist)
-        if rank == 0:
-            print(json.dumps(res), flush=True)
+        if world == 1:
+            res = run_xcb(a, cfg, rank, world, dist)
+            if rank == 0:
+                print(json.dumps(res), flush=True)
+        else:
+            layer = make_ep_layer(cfg, rank, world)
+            for name in names:            # one JSON line per configuration, configuration 5 first
+                res = run_xcb_ep(a, config_for(name, a.experts, a.tokens), rank, world, dist, layer)
+                if rank == 0:
+                    print(json.dumps(res), flush=True)
     finally:
+        if layer is not None:
+            layer.close()  # the peer exchange's buffers (collective)
         if dist:
             dist.destroy_process_group()
 

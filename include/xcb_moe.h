@@ -41,6 +41,10 @@ extern "C" {
 #define XCB_FLAG_POST_NORM 1        /* reference contract: y *= (1 + post_norm_w); out = sum w * y / rms(y) */
 #define XCB_FLAG_DECODE_PATH 2      /* force the decode kernel (default below 257 routes and 33 tokens)       */
 #define XCB_FLAG_PREFILL_PATH 4     /* force the prefill path: tcgen05 grouped GEMMs (default above)         */
+#define XCB_FLAG_DETERMINISTIC 16   /* prefill path: combine the routes in a separate pass, in slot order, so the
+                                       output is bit-reproducible; by default (without the post-norm) the down
+                                       projection adds w * y into a fp32 accumulator itself, whose order of
+                                       additions varies from run to run                                       */
 #define XCB_FLAG_PDL 8              /* single-launch decode calls use programmatic dependent launch: the kernel
                                        may start before the previous kernel of the stream ends and waits
                                        (griddepcontrol.wait) before its first global read; the reference's

@@ -130,27 +130,57 @@ def test_prefill_matches_decode_path(dev):
     assert rel < 5e-3
 
 
-def test_prefill_repeat_and_graph_capture(dev):
+@pytest.mark.parametrize("deterministic", [True, False])
+def test_prefill_repeat_and_graph_capture(dev, deterministic):
+    """Repeated calls and a CUDA-graph replay: bit-identical with the fixed-order combine pass; with the combine
+    fused into the down projection (fp32 reductions in a varying order) within the tolerance."""
     from xcalibur_b200 import PreparedMoE, synth
 
     weights = synth.make_weights(32, 1024, 512, seed=500, device=dev)
     x, logits = synth.make_inputs(333, 1024, 32, seed=501, device=dev)
     layer = PreparedMoE(*weights.values())
-    outs = [layer.forward(x, logits, 4).clone() for _ in range(2)]        # 1332 routes: prefill path by default
-    assert torch.equal(outs[0], outs[1])
+    fwd = lambda: layer.forward(x, logits, 4, deterministic=deterministic)
+    outs = [fwd().clone() for _ in range(2)]        # 1332 routes: prefill path by default
+
+    def same(a, b):
+        if deterministic:
+            return torch.equal(a, b)
+        return torch.allclose(a.float(), b.float(), rtol=1e-2, atol=1e-2)
+
+    assert same(outs[0], outs[1])
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
-        static_out = layer.forward(x, logits, 4)
+        static_out = fwd()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
-            static_out = layer.forward(x, logits, 4)
+            static_out = fwd()
     torch.cuda.current_stream().wait_stream(s)
     for _ in range(2):
         g.replay()
     torch.cuda.synchronize()
-    assert torch.equal(static_out, outs[0])
+    assert same(static_out, outs[0])
     assert layer.check_device_status() == 0
+
+
+def test_fused_combine_matches_the_fixed_order_pass(dev):
+    """The weighted combine fused into the down projection against the separate fixed-order pass, and both against
+    the oracle (Qwen3-shaped experts, 700 tokens, skewed router)."""
+    from xcalibur_b200 import PreparedMoE, synth
+
+    weights = synth.make_weights(128, 2048, 768, seed=510, device=dev)
+    x, logits = synth.make_inputs(700, 2048, 128, seed=511, device=dev, bias_std=0.5)
+    layer = PreparedMoE(*weights.values())
+    fused, ids, wts = layer.forward(x, logits, 8, return_routing=True)
+    fixed = layer.forward(x, logits, 8, deterministic=True)
+    torch.cuda.synchronize()
+    assert layer.check_device_status() == 0
+    assert torch.allclose(fused.float(), fixed.float(), rtol=1e-2, atol=1e-2)
+    rows = sample_rows(to_np(ids))
+    sel = torch.as_tensor(rows, device=dev)
+    want = oracle_layer(x.index_select(0, sel), weights, to_np(ids)[rows], to_np(wts)[rows])
+    assert_close_bf16(fused.index_select(0, sel), want)
+    assert_close_bf16(fixed.index_select(0, sel), want)
 
 
 @pytest.mark.parametrize("T,k,E,ties", [(600, 4, 64, False), (3000, 8, 256, True), (1100, 3, 40, False)])

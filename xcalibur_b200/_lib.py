@@ -28,6 +28,7 @@ XCB_FLAG_POST_NORM = 1
 XCB_FLAG_DECODE_PATH = 2
 XCB_FLAG_PREFILL_PATH = 4
 XCB_FLAG_PDL = 8
+XCB_FLAG_DETERMINISTIC = 16
 XCB_STATIC_SCRATCH_BYTES = 8 << 20
 
 # every symbol include/xcb_moe.h declares

@@ -120,7 +120,8 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   if (have_logits == have_ids) return XCB_ERR_INVALID_ARG;
   const bool post_norm = (a->flags & XCB_FLAG_POST_NORM) != 0;
   if (post_norm && !w->post_norm_w) return XCB_ERR_INVALID_ARG;
-  if (a->flags & ~(XCB_FLAG_POST_NORM | XCB_FLAG_DECODE_PATH | XCB_FLAG_PREFILL_PATH | XCB_FLAG_PDL))
+  if (a->flags &
+      ~(XCB_FLAG_POST_NORM | XCB_FLAG_DECODE_PATH | XCB_FLAG_PREFILL_PATH | XCB_FLAG_PDL | XCB_FLAG_DETERMINISTIC))
     return XCB_ERR_INVALID_ARG;
   if ((a->flags & XCB_FLAG_DECODE_PATH) && (a->flags & XCB_FLAG_PREFILL_PATH)) return XCB_ERR_INVALID_ARG;
   if (!aligned16(a->hidden_states) || !aligned16(a->out) || !aligned16(w->gate_up) || !aligned16(w->down) ||
@@ -230,6 +231,11 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   wp->xperm = (uint16_t*)(b + L.y);  // gathered rows live in the y region: read by the gate_up GEMM before y is written
   wp->inter = sp->inter;
   wp->y = sp->y;
+  // the down projection adds w * y straight into a fp32 [T, H] accumulator (after the gathered rows in the y region,
+  // which holds R*H*4 bytes: room for T*H*4 more when k >= 2); the post-norm needs every y row whole first, and
+  // XCB_FLAG_DETERMINISTIC asks for the fixed-order combine pass
+  wp->fuse = (!post_norm && a->top_k >= 2 && !(a->flags & XCB_FLAG_DETERMINISTIC)) ? 1 : 0;
+  wp->out32 = (float*)(b + L.y + (size_t)a->tokens * a->top_k * s->hidden * 2);
   wp->ss = rp->ss;
   wp->out = a->out;
   wp->T = a->tokens;

@@ -95,6 +95,11 @@ struct WideParams {
   uint16_t* inter;         // mode 0 output, bf16 [routes, I]
   float* y;                // mode 1 output, fp32 [routes, H]
   float* ss;               // mode 1 post-norm sums of squares [routes]
+  // mode 1 fused with the weighted combine (fuse != 0): out32[token][h] += w_route * y instead of writing y
+  const int* order;        // permuted position -> flat route (token = route / k)
+  const float* wts;        // flat route weights
+  float* out32;            // fp32 [T, H], zeroed before the launch
+  int k, fuse;
   int* status;
   int* tilectl;            // [2] tiles claimed so far, CTAs finished (zero between launches)
   int E_loc, R, K, I, H;
@@ -119,8 +124,9 @@ struct WidePathParams {
   uint16_t* inter;
   float* y;
   float* ss;
+  float* out32;            // fp32 [T, H] accumulator of the fused combine (fuse != 0)
   uint16_t* out;
-  int T, k, H, I, E_loc, post_norm;
+  int T, k, H, I, E_loc, post_norm, fuse;
   unsigned long long timeout_ns;
 };
 

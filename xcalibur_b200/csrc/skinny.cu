@@ -70,6 +70,12 @@ __device__ unsigned long long g_trace[1024 * kTraceSlots];
 #define TRACE_ONCE(slot) ((void)0)
 #endif
 
+#ifndef XCB_SK_WAVES
+#define XCB_SK_WAVES 2  // job waves of the static schedule
+#endif
+#ifndef XCB_SK_NOCOMPUTE
+#define XCB_SK_NOCOMPUTE 0  // experiments only: skip the slice arithmetic
+#endif
 #ifndef XCB_SK_MUL
 #define XCB_SK_MUL 41  // share permutation multiplier (prime)
 #endif
@@ -80,8 +86,14 @@ constexpr int SK_W_EPI = SK_NW + 2;                     // reduction + epilogue 
 constexpr int SK_NEPI = 2;                              // epilogue warp e takes the flush events f with f % 2 == e
 constexpr int SK_THREADS = (SK_NW + 2 + SK_NEPI) * 32;  // 20 warps: at most 5 per SM sub-partition
 constexpr int SK_SLICE = 576;                           // 512 B of codes + 64 B of scale bytes per 64-k slice
-constexpr int SK_PER_MAX = 7;                           // slices per compute warp per stage
-constexpr int SK_MAX_STAGES = 8;
+#ifndef XCB_SK_PER_MAX
+#define XCB_SK_PER_MAX 7
+#endif
+#ifndef XCB_SK_MAX_STAGES
+#define XCB_SK_MAX_STAGES 8
+#endif
+constexpr int SK_PER_MAX = XCB_SK_PER_MAX;              // slices per compute warp per stage
+constexpr int SK_MAX_STAGES = XCB_SK_MAX_STAGES;
 constexpr int SK_NSLOT = 2;                             // reduction slots
 constexpr int SK_NBUF_MAX = 2;                          // activation buffers
 constexpr int SK_SEG_RING = 64;                         // per-segment completion counters
@@ -116,7 +128,7 @@ struct SkSegments {
   __device__ void init(int njobs, int nA_rb, int nB_rb, int G, int bid) {
     nrbA = nA_rb;
     nrbB = nB_rb;
-    const int W = njobs >= 2 ? 2 : 1;
+    const int W = njobs >= 2 ? XCB_SK_WAVES : 1;
     long long a[4], b[4];
     int f[4], n[4];
 #pragma unroll
@@ -364,6 +376,7 @@ __device__ void sk_route_small(const SkinnyParams& p, SkTables& rt, SkCtl& cb, i
       if (lane == 0) {
         cb.njobs = njobs;
         cb.nroutes = nroutes;
+        TRACE_AT(4);
       }
     }
   } else {
@@ -623,7 +636,9 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
   } else if (p.small_route) {
     sk_route_small(p, rt, cb, reinterpret_cast<int*>(ring));
   }
+  if (tid == 0) TRACE_AT(21);
   __syncthreads();
+  if (tid == 0) TRACE_AT(27);
   if (p.small_route && bid == 0) sk_publish(p, rt, cb);
   if (tid == 0) TRACE_AT(1);
 
@@ -904,7 +919,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
           const uint8_t* sl = ring + (size_t)st * L.slot_bytes + (size_t)warp * PER * SK_SLICE;
           const uint8_t* xs = xrow + (size_t)(my0 % U) * 128;
           TRACE_T0(t_c);
-          sk_run_per(PER, sl, xs, lane, t, sa);
+          if (!XCB_SK_NOCOMPUTE) sk_run_per(PER, sl, xs, lane, t, sa);
           if (warp == 0) {
             __syncwarp();
             if (lane == 0) TRACE_SPAN(ph ? 31 : 23, t_c);

@@ -68,7 +68,8 @@ constexpr size_t kWdOffX = kWdOffB + (size_t)kWdBSt * kWdBBytes;
 constexpr size_t kWdOffBar = kWdOffX + (size_t)kWdXbuf * 4;
 constexpr size_t kWdOffTab = kWdOffBar + (size_t)kWdNBar * 8;
 constexpr size_t kWdOffMisc = kWdOffTab + 2 * 516 * 4;
-constexpr size_t kWdSmem = kWdOffMisc + 64 + 1024;  // + slack to align the base to 1024
+constexpr size_t kWdOffCol = kWdOffMisc + 64;       // fused combine: [2 tiles][kWdTok] token ids, then route weights
+constexpr size_t kWdSmem = kWdOffCol + 2 * kWdTok * 8 + 1024;  // + slack to align the base to 1024
 // Tensor memory (512 columns): the A ring [0, 128), accumulator 0 [128, 320), accumulator 1 [320, 512): the MMAs
 // of tile i + 1 fill one accumulator while the epilogue drains tile i from the other.
 constexpr uint32_t kWdDCol = 32 * kWdASlots;
@@ -422,6 +423,8 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
     // ---------------------------------------------------------------- epilogue: 8 warps, lane quarter x column half
     const int ew = warp - kWdEpiWarp0, wq = warp & 3, chalf = ew >> 2;
     const uint32_t tlane = (uint32_t)(32 * wq) << 16;
+    int* ctok = reinterpret_cast<int*>(sm + kWdOffCol);        // [2][kWdTok]
+    float* cwt = reinterpret_cast<float*>(ctok + 2 * kWdTok);   // [2][kWdTok]
     uint32_t tc = 0;
     WD_PROF_T0(t_all);
     for (uint32_t n = 0;; ++n, ++tc) {
@@ -429,6 +432,15 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
       if (i < 0) break;
       const WdTile t = wd_tile(i, tpre, offs, E, RB);
       const float gsc = p.gs[t.e] * kTwo52;  // loaded while the MMAs run
+      if (p.fuse) {
+        // the tile's tokens and route weights (buffer tc & 1: a warp one tile ahead fills the other buffer; the
+        // barrier below keeps any warp from running two tiles ahead)
+        for (int c = 32 * ew + lane; c < t.n; c += 32 * kWdEpiWarps) {
+          const int f = p.order[t.q0 + c];
+          ctok[(tc & 1) * kWdTok + c] = f / p.k;
+          cwt[(tc & 1) * kWdTok + c] = p.wts[f] * gsc;
+        }
+      }
       WD_PROF_T0(t_d);
       const uint32_t db = tc & 1;
       const bool good = wd_wait(d_full + db, (tc >> 1) & 1, abrt, p);
@@ -471,6 +483,17 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
             }
           }
           named_bar(2 + 2 * chalf + pair, 64);
+        } else if (p.fuse) {
+          // weighted combine fused into the down projection: each column's token gets w * y for this warp's 32
+          // rows (one coalesced 128-byte reduction per column; the order of the k additions is not fixed)
+          const int h = 128 * t.rb + 32 * wq + lane;
+          const int* tk = ctok + (tc & 1) * kWdTok;
+          const float* wk = cwt + (tc & 1) * kWdTok;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int n = c0 + j;
+            if (n < t.n) atomicAdd(p.out32 + (size_t)tk[n] * p.H + h, __uint_as_float(v[j]) * wk[n]);
+          }
         } else {
           const int h = 128 * t.rb + 32 * wq + lane;
           const float sc = gsc * (p.post_norm ? 1.f + bf2f(p.normw[h]) : 1.f);
@@ -517,7 +540,7 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
 
 // ------------------------------------------------------------------------------------------------ gather / combine
 __global__ void gather_kernel(const uint16_t* __restrict__ x, const int* __restrict__ order, const int* ctl, int k,
-                              int H, uint16_t* __restrict__ xp) {
+                              int H, uint16_t* __restrict__ xp, float* __restrict__ zero, size_t nzero4) {
   const int nroutes = ctl[kCtlRoutes];
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -526,6 +549,20 @@ __global__ void gather_kernel(const uint16_t* __restrict__ x, const int* __restr
     const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(order[q] / k) * H);
     uint4* dst = reinterpret_cast<uint4*>(xp + (size_t)q * H);
     for (int v = lane; v < nv; v += 32) dst[v] = __ldg(src + v);
+  }
+  // the fused combine's fp32 accumulator starts at zero
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nzero4; i += (size_t)gridDim.x * blockDim.x)
+    reinterpret_cast<float4*>(zero)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// out = bf16(out32), 4 values per thread (the end of the fused combine)
+__global__ void to_bf16_kernel(const float* __restrict__ out32, size_t n4, uint16_t* __restrict__ out) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+    const float4 a = __ldcs(reinterpret_cast<const float4*>(out32) + i);
+    uint2 o;
+    o.x = (uint32_t)f2bf(a.x) | ((uint32_t)f2bf(a.y) << 16);
+    o.y = (uint32_t)f2bf(a.z) | ((uint32_t)f2bf(a.w) << 16);
+    reinterpret_cast<uint2*>(out)[i] = o;
   }
 }
 
@@ -614,7 +651,9 @@ int launch_wide_path(const WidePathParams& a, cudaStream_t stream) {
   if (cudaFuncSetAttribute(wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kWdSmem) != cudaSuccess)
     return XCB_ERR_CUDA;
   const int R = a.T * a.k;
-  gather_kernel<<<sms * 4, 256, 0, stream>>>(a.x, a.order, a.ctl, a.k, a.H, a.xperm);
+  const size_t n4 = (size_t)a.T * a.H / 4;
+  gather_kernel<<<sms * 4, 256, 0, stream>>>(a.x, a.order, a.ctl, a.k, a.H, a.xperm, a.fuse ? a.out32 : nullptr,
+                                              a.fuse ? n4 : 0);
   if (cudaGetLastError() != cudaSuccess) return XCB_ERR_CUDA;
 
   WideParams g{};
@@ -630,6 +669,10 @@ int launch_wide_path(const WidePathParams& a, cudaStream_t stream) {
   g.inter = a.inter;
   g.y = a.y;
   g.ss = a.ss;
+  g.order = a.order;
+  g.wts = a.wts;
+  g.out32 = a.out32;
+  g.k = a.k;
 
   g.w = a.wA;
   g.gs = a.gsA;
@@ -644,10 +687,14 @@ int launch_wide_path(const WidePathParams& a, cudaStream_t stream) {
   g.R = a.H;
   g.K = a.I;
   g.mode = 1;
+  g.fuse = a.fuse;
   rc = launch_wide_gemm(g, a.inter, R, a.I, sms, stream);
   if (rc != XCB_OK) return rc;
 
-  combine_kernel<<<sms * 8, 256, 0, stream>>>(a.y, a.wts, a.pos, a.ss, a.T, a.k, a.H, a.post_norm, a.out);
+  if (a.fuse)
+    to_bf16_kernel<<<sms * 8, 256, 0, stream>>>(a.out32, n4, a.out);
+  else
+    combine_kernel<<<sms * 8, 256, 0, stream>>>(a.y, a.wts, a.pos, a.ss, a.T, a.k, a.H, a.post_norm, a.out);
   return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
 }
 

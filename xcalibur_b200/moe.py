@@ -158,14 +158,16 @@ class PreparedMoE:
     def build_call(self, hidden_states: torch.Tensor, router_logits: Optional[torch.Tensor] = None, top_k: int = 8,
                    *, topk_ids: Optional[torch.Tensor] = None, topk_weights: Optional[torch.Tensor] = None,
                    post_norm: bool = False, out: Optional[torch.Tensor] = None, return_routing: bool = False,
-                   path: str = "auto", wait_limit_us: int = 0, pdl: bool = False):
+                   path: str = "auto", wait_limit_us: int = 0, pdl: bool = False, deterministic: bool = False):
         """Validate one call and bind its buffers; returns a ``LayerCall`` whose ``launch()`` enqueues it.
 
         ``path``: "auto" (the library picks by batch size), "decode" (the streaming decode kernel) or "prefill"
         (the tensor-core grouped GEMMs).  ``wait_limit_us``: bound of every device-side wait of the call (0: the
         library's 2 s); a wait that runs out sets XCB_STATUS_DEVICE_TIMEOUT (``check_device_status``).  ``pdl``:
         launch a single-launch decode call with programmatic dependent launch (it may start while the previous
-        kernel of the stream finishes, and waits for it before reading anything)."""
+        kernel of the stream finishes, and waits for it before reading anything).  ``deterministic``: on the
+        prefill path, combine the routes in a separate fixed-order pass (bit-reproducible output) instead of inside
+        the down projection."""
         x = hidden_states
         if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != self.H:
             raise ValueError(f"hidden_states must be bf16 [T, {self.H}]")
@@ -200,6 +202,7 @@ class PreparedMoE:
         if path not in _PATH_FLAGS:
             raise ValueError(f"path must be one of {sorted(_PATH_FLAGS)}")
         flags = (_lib.XCB_FLAG_POST_NORM if post_norm else 0) | _PATH_FLAGS[path] | (_lib.XCB_FLAG_PDL if pdl else 0)
+        flags |= _lib.XCB_FLAG_DETERMINISTIC if deterministic else 0
         if wait_limit_us < 0:
             raise ValueError("wait_limit_us must be >= 0")
         args = XcbMoeArgs(T, top_k, flags, int(wait_limit_us), x.data_ptr(), _ptr(logits),
@@ -209,10 +212,10 @@ class PreparedMoE:
     def forward(self, hidden_states: torch.Tensor, router_logits: Optional[torch.Tensor] = None, top_k: int = 8, *,
                 topk_ids: Optional[torch.Tensor] = None, topk_weights: Optional[torch.Tensor] = None,
                 post_norm: bool = False, out: Optional[torch.Tensor] = None, return_routing: bool = False,
-                path: str = "auto", wait_limit_us: int = 0, pdl: bool = False):
+                path: str = "auto", wait_limit_us: int = 0, pdl: bool = False, deterministic: bool = False):
         call = self.build_call(hidden_states, router_logits, top_k, topk_ids=topk_ids, topk_weights=topk_weights,
                                post_norm=post_norm, out=out, return_routing=return_routing, path=path,
-                               wait_limit_us=wait_limit_us, pdl=pdl)
+                               wait_limit_us=wait_limit_us, pdl=pdl, deterministic=deterministic)
         call.launch()
         return call.result()
 

@@ -56,11 +56,13 @@ def make_weights(E: int, H: int, I: int, seed: int = 0, device="cuda", std: floa
     return out
 
 
-def make_inputs(T: int, H: int, E: int, seed: int = 1, device="cuda", bias_std: float = 0.0, zipf_s: float = 0.0):
+def make_inputs(T: int, H: int, E: int, seed: int = 1, device="cuda", bias_std: float = 0.0, zipf_s: float = 0.0,
+                zipf_order_seed=None):
     """bf16 N(0,1) activations [T, H] and fp32 router logits [T, E] (N(0,1) + per-expert bias).
 
-    ``bias_std``: bias ~ N(0, bias_std) per expert (mildly uneven loads).  ``zipf_s``: bias_e = -s * ln(e + 1), a
-    Zipf-like skew toward low expert ids (the worst case for contiguous expert sharding)."""
+    ``bias_std``: bias ~ N(0, bias_std) per expert (mildly uneven loads).  ``zipf_s``: bias_e = -s * ln(r_e + 1), a
+    Zipf-like skew, with r_e = e (toward low expert ids: the worst case for contiguous expert sharding) or, with
+    ``zipf_order_seed``, expert e's place in a seeded random order (the same on every rank and call)."""
     device = torch.device(device)
     g = torch.Generator(device=device)
     g.manual_seed(seed)
@@ -69,7 +71,12 @@ def make_inputs(T: int, H: int, E: int, seed: int = 1, device="cuda", bias_std: 
     if bias_std:
         logits += torch.randn((1, E), generator=g, device=device, dtype=torch.float32) * bias_std
     if zipf_s:
-        logits += (-zipf_s * torch.log(torch.arange(1, E + 1, device=device, dtype=torch.float32)))[None, :]
+        r = torch.arange(E, device=device)
+        if zipf_order_seed is not None:
+            gp = torch.Generator(device="cpu")
+            gp.manual_seed(int(zipf_order_seed))
+            r = torch.randperm(E, generator=gp).to(device)
+        logits += (-zipf_s * torch.log(r.to(torch.float32) + 1.0))[None, :]
     return x, logits
 
 
