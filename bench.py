@@ -84,6 +84,8 @@ def parse():
     ap.add_argument("--tokens", type=int, default=0, help="override the token count (small profiling cases)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--pdl", type=int, default=0, help="1: decode steps use programmatic dependent launch")
+    ap.add_argument("--path", default="auto", choices=["auto", "decode", "prefill"],
+                    help="okc configurations: force this library's decode or prefill path")
     return ap.parse_args()
 
 
@@ -697,8 +699,15 @@ def run_okc(a, cfg):
         from xcalibur_b200 import kernel_fn, prepare
 
         state = prepare(weights, local_start=0, local_count=32, n_experts=256)
-        fn = lambda d: kernel_fn(d, state)
-        launches = 1 if T * 8 <= 256 and T <= 32 else 5
+        if a.path == "auto":
+            fn = lambda d: kernel_fn(d, state)
+        else:
+            lay = state["layer"]
+            fn = lambda d: lay.forward(d["hidden_states"], None, topk_ids=d["topk_ids"],
+                                       topk_weights=d["topk_weights"], post_norm=True, path=a.path)
+        # decode kernel alone (in-kernel routing), router + decode kernel (up to ~192 expected held routes), or
+        # router + gather + two grouped GEMMs + final pass
+        launches = 1 if T * 8 <= 256 and T <= 32 else (2 if T * 8 * 32 // 256 <= 192 else 5)
         what = "xcalibur_b200 kernel_fn"
     del weights
     torch.cuda.empty_cache()

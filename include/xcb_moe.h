@@ -39,7 +39,9 @@ extern "C" {
 
 /* ---- forward flags ---- */
 #define XCB_FLAG_POST_NORM 1        /* reference contract: y *= (1 + post_norm_w); out = sum w * y / rms(y) */
-#define XCB_FLAG_DECODE_PATH 2      /* force the decode kernel (default below 257 routes and 33 tokens)       */
+#define XCB_FLAG_DECODE_PATH 2      /* force the decode kernel (default below 257 routes and 33 tokens; for a
+                                       layer holding some of the router's experts, up to ~192 expected held
+                                       routes)                                                                  */
 #define XCB_FLAG_PREFILL_PATH 4     /* force the prefill path: tcgen05 grouped GEMMs (default above)         */
 #define XCB_FLAG_DETERMINISTIC 16   /* prefill path: combine the routes in a separate pass, in slot order, so the
                                        output is bit-reproducible; by default (without the post-norm) the down

@@ -93,6 +93,7 @@ namespace {
 // Routes per call from which xcb_moe_forward takes the prefill path (tensor-core grouped GEMMs) instead of the
 // decode kernel, unless a XCB_FLAG_*_PATH flag forces one.
 constexpr long long kPrefillMinRoutes = kSmallRoutes + 1;
+constexpr long long kShardDecodeMaxRoutes = 192;  // expected held routes up to which a shard stays on the decode path
 
 struct CallPlan {
   RouteParams rp;
@@ -131,8 +132,16 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   if (ws_bytes < L.total) return XCB_ERR_WORKSPACE;
   uint8_t* b = (uint8_t*)ws;
   const long long routes = (long long)a->tokens * a->top_k;
+  // A layer that holds only some of the router's experts (an expert-parallel shard, the reference's local range)
+  // sees about routes * held / total of them: the decode kernel streams each held expert once per job of up to 8
+  // tokens, and stays ahead of the tensor-core path up to ~192 such routes (measured at the reference's shape:
+  // 128 tokens x top-8 over 32 of 256 experts 280 us against 359 us; 256 tokens 384 against 369 us).
+  const bool shard = s->num_experts < s->total_experts;
+  const long long est_local = routes * s->num_experts / s->total_experts;
   plan->wide = (a->flags & XCB_FLAG_PREFILL_PATH) ||
-               (!(a->flags & XCB_FLAG_DECODE_PATH) && (routes >= kPrefillMinRoutes || a->tokens > kSmallTokens));
+               (!(a->flags & XCB_FLAG_DECODE_PATH) &&
+                (shard ? est_local > kShardDecodeMaxRoutes
+                       : (routes >= kPrefillMinRoutes || a->tokens > kSmallTokens)));
   if (!plan->wide && !skinny_supported(s->hidden, s->inter)) {
     // no stage plan of the decode kernel fits this shape: the tensor-core path serves every batch size
     if (a->flags & XCB_FLAG_DECODE_PATH) return XCB_ERR_UNSUPPORTED;
