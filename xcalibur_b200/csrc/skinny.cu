@@ -43,18 +43,23 @@ namespace xcb {
 
 // Optional timeline trace, read back with xcb_trace_read (off in the shipped library): -DXCB_TRACE=1 records
 // %globaltimer stamps, clock64 spans and counters per CTA; -DXCB_TRACE=2 only each CTA's start and exit times and
-// its SM (light enough not to change the timing).
+// its SM (light enough not to change the timing); -DXCB_TRACE=3 the stamps of mode 1 with the clock64 spans and
+// counters summed in per-thread registers and written once at kernel end.
 #ifndef XCB_TRACE
 #define XCB_TRACE 0
 #endif
 #if XCB_TRACE
-constexpr int kTraceSlots = 32;
+constexpr int kTraceSlots = 48;
 __device__ unsigned long long g_trace[1024 * kTraceSlots];
 #define TRACE_EDGE(slot) (g_trace[blockIdx.x * kTraceSlots + (slot)] = gtimer())
 #endif
-#if XCB_TRACE == 1
+#if XCB_TRACE == 1 || XCB_TRACE == 3
 #define TRACE_AT(slot) (g_trace[blockIdx.x * kTraceSlots + (slot)] = gtimer())
+#if XCB_TRACE == 1
 #define TRACE_ADD(slot, v) atomicAdd(&g_trace[blockIdx.x * kTraceSlots + (slot)], (unsigned long long)(v))
+#else
+#define TRACE_ADD(slot, v) (tr_acc[(slot)] += (unsigned long long)(v))
+#endif
 #define TRACE_GET(slot) (*(volatile unsigned long long*)&g_trace[blockIdx.x * kTraceSlots + (slot)])
 #define TRACE_T0(name) const unsigned long long name = clock64()
 #define TRACE_SPAN(slot, name) TRACE_ADD(slot, clock64() - (name))
@@ -574,7 +579,10 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
   // one token and one row per job (so not an expert named twice by precomputed routing): every phase-A segment
   // uses that token's row, staged before routing into row 0 of buffers 0 and 1
   const bool xpre = p.T == 1;
-#if XCB_TRACE == 1
+#if XCB_TRACE == 3
+  unsigned long long tr_acc[kTraceSlots] = {};  // spans and counters of this thread
+#endif
+#if XCB_TRACE == 1 || XCB_TRACE == 3
   unsigned trace_once = 0;  // TRACE_ONCE slots this thread has stamped
 #endif
 
@@ -698,6 +706,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
     // ------------------------------------------------------------------ activation staging + f16 conversion
     int k = 0;                 // non-empty segments so far
     uint32_t land0 = 0, land1 = 0;  // landings per buffer (phase parity of act_land)
+    TRACE_T0(t_act);
     for (int s = 0; s < nseg; ++s) {
       int ph, job;
       long long u0, u1;
@@ -733,9 +742,15 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
       }
       __syncwarp();
       const uint32_t lpar = (b ? land1++ : land0++) & 1;
+      TRACE_T0(t_al);
       mbar_wait(cb.act_land + b, lpar, p.timeout_ns, status);
-      if (lane == 0) TRACE_ONCE(17);
+      if (lane == 0) {
+        TRACE_ONCE(17);
+        TRACE_SPAN(35, t_al);
+      }
+      TRACE_T0(t_cv);
       sk_rows_to_f16(dst, L.pitch, ntok, K, cb.xexp[b]);
+      if (lane == 0) TRACE_SPAN(36, t_cv);
       __syncwarp();
       if (lane == 0) {
         TRACE_ONCE(16);
@@ -743,7 +758,10 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
       }
       ++k;
     }
-    if (lane == 0) TRACE_AT(20);
+    if (lane == 0) {
+      TRACE_AT(20);
+      TRACE_SPAN(37, t_act);
+    }
   } else if (warp >= SK_W_EPI) {
     // ------------------------------------------------------------------ reduction + epilogue
     // slot lane l holds the partial of accumulator lane (g, t) = (l % 8, l / 8): rows g, g + 8; tokens 2t, 2t + 1
@@ -751,6 +769,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
     const int g = lane & 7, t = lane >> 3;
     const bool act = lane < L.rl;
     int f = 0, k = 0;
+    TRACE_T0(t_epi);
     for (int s = 0; s < nseg; ++s) {
       int ph, job;
       long long u0, u1;
@@ -772,6 +791,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
           TRACE_SPAN(24, t_sl);
           TRACE_ADD(26, 1);
         }
+        TRACE_T0(t_ew);
         const float* sb = red + slot * (L.red_slot / 4);
         const int i0 = ev * upe, i1 = min(nunits, i0 + upe);
         for (int i = i0; i < i1; ++i) {
@@ -834,6 +854,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
           }
           done = __shfl_sync(0xffffffffu, done, 0);
           if (done == nunits) {
+            TRACE_T0(t_sc);
             __threadfence();
             if (lane == 0) cb.seg_cnt[k % SK_SEG_RING] = 0;
             if (ph == 0) {
@@ -846,12 +867,17 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
               }
             }
             __syncwarp();
+            if (lane == 0) TRACE_SPAN(34, t_sc);
           }
         }
+        if (lane == 0) TRACE_SPAN(ph ? 33 : 32, t_ew);
       }
       ++k;
     }
-    if (lane == 0) TRACE_AT(22);
+    if (lane == 0) {
+      TRACE_AT(22);
+      TRACE_SPAN(41, t_epi);
+    }
   } else {
     // ------------------------------------------------------------------ compute warps
     // Stage i of a segment holds slices [i SS, i SS + ns); warp w takes [i SS + w PER, + PER), all in one unit.
@@ -881,6 +907,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
       if (lane == 0) mbar_arrive(cb.slot_full + slot);
       pend = false;
     };
+    TRACE_T0(t_cw);
     for (int s = 0; s < nseg; ++s) {
       int ph, job;
       long long u0, u1;
@@ -960,6 +987,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
       }
       ++k;
     }
+    if (warp == 0 && lane == 0) TRACE_SPAN(40, t_cw);
   }
 
   if (tid == 0) TRACE_AT(7);
@@ -1030,6 +1058,10 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
     }
   }
 
+#if XCB_TRACE == 3
+  for (int s = 0; s < kTraceSlots; ++s)
+    if (tr_acc[s]) atomicAdd(&g_trace[blockIdx.x * kTraceSlots + s], tr_acc[s]);
+#endif
   // -------------------------------------------------------------------- exit: the last CTA resets the counters
   __syncthreads();
   if (tid == 0) {
