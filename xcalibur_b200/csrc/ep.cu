@@ -302,9 +302,13 @@ __global__ void ep_p2p_dispatch_kernel(const uint16_t* __restrict__ x, const flo
       dw[t * k + lane] = w;
     }
   }
-  __threadfence_system();
+  // the block's stores, then one system-scope fence and the release by thread 0 (the barrier orders every thread's
+  // stores before it; a fence in every thread would wait for NVLink acknowledgements 256 times over)
   __syncthreads();
-  if (threadIdx.x == 0) p2p_red_release(reinterpret_cast<unsigned*>(dst + L.flag) + rank, 1u);
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    p2p_red_release(reinterpret_cast<unsigned*>(dst + L.flag) + rank, 1u);
+  }
   // one block waits for every peer's rows in this rank's buffer; the kernels after this one read them
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     p2p_wait_all(reinterpret_cast<const unsigned*>(mine + L.flag), G, e * (unsigned)nb, timeout_ns, status);
@@ -327,10 +331,10 @@ __global__ void ep_p2p_combine_kernel(const uint16_t* __restrict__ parts, int T,
   const uint4* src = reinterpret_cast<const uint4*>(parts + (size_t)d * T * H);
   uint4* dp = reinterpret_cast<uint4*>(dst + L.part + (size_t)rank * T * H * 2);
   for (int i = r0 * nv + threadIdx.x; i < r1 * nv; i += blockDim.x) dp[i] = __ldg(src + i);
-  __threadfence_system();
-  __syncthreads();
+  __syncthreads();  // as in the dispatch: the block's stores, then one fence and the release by thread 0
   __shared__ int ok;
   if (threadIdx.x == 0) {
+    __threadfence_system();
     p2p_red_release(reinterpret_cast<unsigned*>(dst + L.flag) + G + rank, 1u);
     ok = p2p_wait_all(reinterpret_cast<const unsigned*>(mine + L.flag) + G, G, e * (unsigned)nb, timeout_ns, status);
     // a dispatch of this step that timed out left the local layer with incomplete rows: the sums are invalid too
