@@ -45,13 +45,25 @@
 
 namespace xcb {
 
-constexpr int kWdTok = 192;       // tokens per tile (MMA N upper bound; two accumulators of this width)
+// Tile shape knobs (compile time): tokens per tile, tensor-memory A slots, activation stages.  Tensor memory holds
+// the A ring (32 columns a slot) and two accumulators of kWdTok columns: 4 x 32 + 2 x 192 = 512.
+#ifndef XCB_WD_TOK
+#define XCB_WD_TOK 192
+#endif
+#ifndef XCB_WD_ASLOTS
+#define XCB_WD_ASLOTS 4
+#endif
+#ifndef XCB_WD_BST
+#define XCB_WD_BST 4
+#endif
+constexpr int kWdTok = XCB_WD_TOK;  // tokens per tile (MMA N upper bound; two accumulators of this width)
 constexpr int kWdStage = 18432;   // packed bytes of 256 k x 128 rows
 constexpr int kWdChunk = 4608;    // packed bytes of 64 k x 128 rows
 constexpr int kWdWSt = 4;         // weight ring stages (power of two)
-constexpr int kWdBSt = 4;         // activation ring stages, 64 k x 256 rows bf16 each
-constexpr int kWdBBytes = 32768;
-constexpr int kWdASlots = 4;      // tensor-memory A ring, 32 columns each (power of two)
+constexpr int kWdBSt = XCB_WD_BST;  // activation ring stages, 64 k x (the widest box) bf16 each
+constexpr int kWdBBytes = (kWdTok > 128 ? 256 : (kWdTok > 64 ? 128 : 64)) * 128;
+constexpr int kWdASlots = XCB_WD_ASLOTS;  // tensor-memory A ring, 32 columns each (power of two)
+constexpr int kWdEpiHalf = kWdTok > 128 ? 128 : kWdTok / 2;  // columns of one epilogue column half
 #ifndef XCB_WD_NDQ
 #define XCB_WD_NDQ 2
 #endif
@@ -453,8 +465,8 @@ __global__ void __launch_bounds__(kWdThreads, 1) wide_kernel(const WideParams p,
       named_bar(1, 32 * kWdEpiWarps);  // the epilogue warps leave together when any of them gave up
       if (*abrt) break;
       tc_fence_after();
-      const int cend = min(t.n, 128 * chalf + 128);
-      for (int c0 = 128 * chalf; c0 < cend; c0 += 32) {
+      const int cend = min(t.n, kWdEpiHalf * (chalf + 1));
+      for (int c0 = kWdEpiHalf * chalf; c0 < cend; c0 += 32) {
         uint32_t v[32];
         WD_PROF_T0(t_l);
         tc_ld_x32(tmem + tlane + kWdDCol + db * kWdTok + c0, v);
