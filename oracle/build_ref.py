@@ -22,7 +22,8 @@ Outputs go to ``oracle/_ref/`` only: one ``.so`` per build and ``manifest.json``
 defines).  The intermediate sources stay in a temporary directory and are deleted; nothing of the reference's
 source enters this repository.  ``oracle/okc_ref.py`` loads the modules on the GPU box.
 
-Run:  python oracle/build_ref.py --reference /path/to/xCalibur   (a few minutes: five nvcc builds)
+Run:  python oracle/build_ref.py --reference /path/to/xCalibur   (five nvcc builds of ~4 minutes each, run as
+parallel processes by ``build_parallel``; ``--only NAME`` builds one)
 """
 from __future__ import annotations
 
@@ -31,12 +32,14 @@ import hashlib
 import json
 import os
 import shutil
+import subprocess
 import sys
 import tempfile
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
 SFX = ("-DOKC_PRMTSC=1",)
+NAMES = ("tiny", "tiny2", "mid", "main", "program")
 
 
 def _variants(m):
@@ -66,7 +69,9 @@ def up_to_date(ref_root: str) -> bool:
         os.path.exists(os.path.join(OUT, v["so"])) for v in d["builds"].values())
 
 
-def build(ref_root: str, only=None, verbose: bool = False) -> dict:
+def build(ref_root: str, only=None, verbose: bool = False, manifest_path=None) -> dict:
+    """Build the named variants (all when ``only`` is None).  The manifest goes to ``manifest_path`` when given (one
+    process's part of a parallel build), else it is merged into oracle/_ref/manifest.json."""
     import torch
     from torch.utils import cpp_extension
 
@@ -113,6 +118,10 @@ def build(ref_root: str, only=None, verbose: bool = False) -> dict:
         torch.cuda.get_device_capability = saved_cap
         m._xc_load_inline = saved_li
         shutil.rmtree(tmp, ignore_errors=True)
+    if manifest_path:
+        with open(manifest_path, "w") as f:
+            json.dump(manifest, f, indent=1)
+        return manifest
     if only and os.path.exists(os.path.join(OUT, "manifest.json")):
         with open(os.path.join(OUT, "manifest.json")) as f:
             old = json.load(f)
@@ -124,10 +133,43 @@ def build(ref_root: str, only=None, verbose: bool = False) -> dict:
     return manifest
 
 
+def build_parallel(ref_root: str, verbose: bool = False) -> dict:
+    """All variants, one process each (the nvcc builds are single-threaded), then one merged manifest."""
+    parts = tempfile.mkdtemp(prefix="xcb_refparts_")
+    try:
+        procs = {}
+        for name in NAMES:
+            cmd = [sys.executable, os.path.abspath(__file__), "--reference", ref_root, "--only", name,
+                   "--manifest", os.path.join(parts, name + ".json")] + (["--verbose"] if verbose else [])
+            procs[name] = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+        failed = []
+        for name, pr in procs.items():
+            out, _ = pr.communicate()
+            if pr.returncode != 0:
+                failed.append(f"{name} (exit {pr.returncode}): {out[-2000:]}")
+            else:
+                print(out.strip(), flush=True)
+        if failed:
+            raise RuntimeError("reference builds failed: " + " | ".join(failed))
+        manifest = {"source_sha256": source_digest(ref_root), "arch": "sm_100", "builds": {}}
+        for name in NAMES:
+            with open(os.path.join(parts, name + ".json")) as f:
+                manifest["builds"].update(json.load(f)["builds"])
+        with open(os.path.join(OUT, "manifest.json"), "w") as f:
+            json.dump(manifest, f, indent=1)
+        return manifest
+    finally:
+        shutil.rmtree(parts, ignore_errors=True)
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("XCB_REFERENCE", "/root/reference"))
     ap.add_argument("--only", nargs="*", default=None)
     ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--manifest", default=None, help="write this build's manifest here (a parallel build's part)")
     a = ap.parse_args()
-    build(a.reference, a.only, a.verbose)
+    if a.only is None and a.manifest is None:
+        build_parallel(a.reference, a.verbose)
+    else:
+        build(a.reference, a.only, a.verbose, a.manifest)
