@@ -243,6 +243,32 @@ def test_deepseek_decode_parity(dev, T):
     assert_close_bf16(out, oracle_layer(x, weights, want_ids, want_w))
 
 
+@pytest.mark.parametrize("source", ["logits", "given", "given_pdl"])
+def test_deepseek_decode_two_tokens(dev, source):
+    """Two tokens at the C2 shape (H=7168, I=2048, top-8): every job holds one token, so the decode kernel stages
+    both token rows at start and each phase-A segment reads its token's row (the shape of the expert-parallel decode
+    step's local layer at two ranks).  With 16 experts the two tokens share several, so segments of either token
+    follow each other in any order; routes from the router, given, and given with PDL."""
+    from xcalibur_b200 import PreparedMoE
+
+    weights, x, logits = _synthetic(16, 7168, 2048, 2, 130, dev)
+    layer = PreparedMoE(*weights.values())
+    if source == "logits":
+        out, ids, wts = layer.forward(x, logits, 8, return_routing=True)
+        want_ids, want_w = moe_ref.route_topk(to_np(logits), 8)
+        torch.cuda.synchronize()
+        assert np.array_equal(to_np(ids), want_ids)
+    else:
+        rng = np.random.default_rng(131)
+        want_ids = np.stack([rng.choice(16, 8, replace=False) for _ in range(2)]).astype(np.int32)
+        want_w = rng.dirichlet(np.ones(8), size=2).astype(np.float32)
+        out = layer.forward(x, None, topk_ids=torch.from_numpy(want_ids).to(dev),
+                            topk_weights=torch.from_numpy(want_w).to(dev), pdl=source == "given_pdl")
+    torch.cuda.synchronize()
+    assert layer.check_device_status() == 0
+    assert_close_bf16(out, oracle_layer(x, weights, want_ids, want_w))
+
+
 @pytest.mark.parametrize("T", [1, 8, 64, 512])
 def test_qwen3_parity(dev, T):
     """C4 shape (H=2048, I=768, E=128, top-8)."""

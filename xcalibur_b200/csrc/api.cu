@@ -215,6 +215,7 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
     sp->job_tokens = (int)(per_job < kJobTokens ? per_job : kJobTokens);
     // the in-kernel router may split jobs finer, so that the shared-memory plan keeps its large stages
     if (small) sp->job_tokens = skinny_job_cap(s->hidden, s->inter, sp->job_tokens, (int)routes);
+    if (small && a->tokens == 2 && skinny_two_one_token_jobs(s->hidden, s->inter, (int)routes)) sp->job_tokens = 1;
   }
   sp->post_norm = post_norm ? 1 : 0;
   sp->grid_combine = (post_norm || !small) ? 1 : 0;

@@ -137,6 +137,7 @@ size_t route_smem_bytes(int E_loc);
 int launch_skinny(const SkinnyParams& p, cudaStream_t stream);
 bool skinny_supported(int H, int I);  // the decode kernel has a stage plan for this shape
 int skinny_job_cap(int H, int I, int want, int route_R);
+bool skinny_two_one_token_jobs(int H, int I, int route_R);
 int launch_pack(const PackParams& p, cudaStream_t stream);
 int launch_quantize(const QuantParams& p, cudaStream_t stream);
 

@@ -565,6 +565,10 @@ __device__ int sk_row_to_f16_warps(uint8_t* row, uint8_t* copy, int K, int* part
   return e;
 }
 
+// TWO: a call of two tokens whose jobs hold one token each, with two activation buffers (the host checks): both
+// token rows are staged at kernel start, token n in buffer n, so the phase-A segments need no staging.  The other
+// instantiation is the general kernel.
+template <bool TWO>
 __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParams p, const SkLayout L) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* ring = smem + L.ring;
@@ -626,6 +630,11 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
       mbar_arrive_expect_tx(&cb.x_land, p.H * 2);
       bulk_g2s(bufs, p.x, p.H * 2, &cb.x_land);
     }
+    if constexpr (TWO) {  // two tokens: row n into buffer n
+      mbar_arrive_expect_tx(&cb.x_land, 2 * p.H * 2);
+      bulk_g2s(bufs, p.x, p.H * 2, &cb.x_land);
+      bulk_g2s(bufs + (size_t)L.rows * L.pitch, p.x + p.H, p.H * 2, &cb.x_land);
+    }
   }
   for (int i = tid; i < SK_SEG_RING; i += SK_THREADS) cb.seg_cnt[i] = 0;
   __syncthreads();  // barrier initialisation visible to every warp
@@ -637,6 +646,15 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
     if (warp == SK_NW - 12 && lane == 0) {
       cb.xexp[0][0] = e;
       cb.xexp[1][0] = e;
+    }
+  }
+  if constexpr (TWO) {
+    if (warp >= SK_NW - 12 && warp < SK_NW) {  // six warps per token row (named barriers 1 and 2)
+      const int w = warp - (SK_NW - 12), n = w / 6;
+      mbar_wait(&cb.x_land, 0, p.timeout_ns, status);
+      const int e = sk_row_to_f16_warps(bufs + (size_t)n * L.rows * L.pitch, nullptr, p.H, cb.xpart + 8 * n, w % 6,
+                                        6, 1 + n);
+      if (w % 6 == 0 && lane == 0) cb.xexp[n][0] = e;
     }
   }
   if (route_one) {
@@ -717,7 +735,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
       const int K = ph ? p.I : p.H;
       const int ntok = min(jb.z, L.rows);
       uint8_t* dst = bufs + (size_t)b * L.rows * L.pitch;
-      if (xpre && ph == 0) {  // phase-A segments precede every phase-B one, so both buffers still hold the row
+      if ((xpre || TWO) && ph == 0) {  // phase-A segments precede every phase-B one: the staged rows stay put
         if (lane == 0) {
           if (k >= NBUF) mbar_wait(cb.act_empty + b, ((k / NBUF) + 1) & 1, p.timeout_ns, status);
           mbar_arrive(cb.act_full + b);
@@ -728,6 +746,9 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
       }
       if (lane == 0) {
         if (k >= NBUF) mbar_wait(cb.act_empty + b, ((k / NBUF) + 1) & 1, p.timeout_ns, status);
+        // two tokens: the previous segment read the buffer of its job's token, whichever that was; both buffers
+        // must be released before the first phase-B staging overwrites one
+        if (TWO && k >= 1) mbar_wait(cb.act_empty + (k - 1) % NBUF, ((k - 1) / NBUF) & 1, p.timeout_ns, status);
         if (ph == 1) {
           TRACE_ONCE(5);
           wait_geq(p.doneA + job, nrbA, p.timeout_ns, status);  // every phase-A unit of this job is published
@@ -931,8 +952,15 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_kernel(const SkinnyParam
       const bool one = p.T == 1;
       const uint8_t* xrow = bufs + (size_t)b * L.rows * L.pitch + (size_t)(g < ntok && !one ? g : 0) * L.pitch;
       // column scales 2^e of this lane's tokens 2t, 2t + 1 (rows past the job's tokens are discarded)
-      const float sc0 = __uint_as_float((uint32_t)(127 + cb.xexp[b][one ? 0 : min(2 * t, ntok - 1)]) << 23);
-      const float sc1 = __uint_as_float((uint32_t)(127 + cb.xexp[b][one ? 0 : min(2 * t + 1, ntok - 1)]) << 23);
+      float sc0 = __uint_as_float((uint32_t)(127 + cb.xexp[b][one ? 0 : min(2 * t, ntok - 1)]) << 23);
+      float sc1 = __uint_as_float((uint32_t)(127 + cb.xexp[b][one ? 0 : min(2 * t + 1, ntok - 1)]) << 23);
+      if constexpr (TWO) {
+        if (ph == 0) {  // the job's one token n = its route's token, staged in buffer n
+          const int n = order[jb.y] / p.k;
+          xrow = bufs + (size_t)n * L.rows * L.pitch;
+          sc0 = sc1 = __uint_as_float((uint32_t)(127 + cb.xexp[n][0]) << 23);
+        }
+      }
       for (int i = 0; i < nst; ++i) {
         TRACE_T0(t_f);
         mbar_wait(cb.full + st, sphase, p.timeout_ns, status);
@@ -1097,7 +1125,9 @@ int skinny_config(int* grid_out, SkLayout* plan, int H, int I, int job_tokens, i
   if (cudaGetDevice(&dev) != cudaSuccess) return XCB_ERR_CUDA;
   const SkLayout L = sk_layout(H, I, job_tokens, route_R);
   if (L.nstage < 3) return XCB_ERR_UNSUPPORTED;
-  if (cudaFuncSetAttribute(skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) != cudaSuccess)
+  if (cudaFuncSetAttribute(skinny_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(skinny_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total) != cudaSuccess)
     return XCB_ERR_CUDA;
   if (dev != cached_dev) {
     if (cudaDeviceGetAttribute(&cached_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return XCB_ERR_CUDA;
@@ -1119,6 +1149,13 @@ int skinny_job_cap(int H, int I, int want, int route_R) {
   return 1;
 }
 
+// Two tokens: one-token jobs are worth an expert the tokens share being streamed twice when they keep two activation
+// buffers and two-token jobs would not.  The kernel then stages both rows at start (the two-token instantiation).
+bool skinny_two_one_token_jobs(int H, int I, int route_R) {
+  const SkLayout one = sk_layout(H, I, 1, route_R), two = sk_layout(H, I, 2, route_R);
+  return one.nstage >= 3 && one.nbuf == 2 && (two.nstage < 3 || two.nbuf < 2);
+}
+
 bool skinny_supported(int H, int I) {
   return sk_layout(H, I, kJobTokens, kSmallRoutes).nstage >= 3 && sk_layout(H, I, 1, kSmallRoutes).nstage >= 3;
 }
@@ -1128,8 +1165,13 @@ int launch_skinny(const SkinnyParams& p, cudaStream_t stream) {
   SkLayout plan;
   int rc = skinny_config(&grid, &plan, p.H, p.I, p.job_tokens, p.small_route ? p.T * p.k : 0);
   if (rc != XCB_OK) return rc;
+  // two tokens with one token per job and two activation buffers: the instantiation that stages both rows at start
+  const bool two = p.T == 2 && plan.rows == 1 && plan.nbuf == 2;
   if (!p.pdl) {
-    skinny_kernel<<<grid, SK_THREADS, plan.total, stream>>>(p, plan);
+    if (two)
+      skinny_kernel<true><<<grid, SK_THREADS, plan.total, stream>>>(p, plan);
+    else
+      skinny_kernel<false><<<grid, SK_THREADS, plan.total, stream>>>(p, plan);
     return cudaGetLastError() == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
   }
   cudaLaunchConfig_t cfg = {};
@@ -1142,7 +1184,9 @@ int launch_skinny(const SkinnyParams& p, cudaStream_t stream) {
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, skinny_kernel, p, plan) == cudaSuccess ? XCB_OK : XCB_ERR_CUDA;
+  return cudaLaunchKernelEx(&cfg, two ? skinny_kernel<true> : skinny_kernel<false>, p, plan) == cudaSuccess
+             ? XCB_OK
+             : XCB_ERR_CUDA;
 }
 
 }  // namespace xcb
