@@ -156,6 +156,7 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
   rp->E_tot = s->total_experts;
   rp->lo = s->expert_offset;
   rp->E_loc = s->num_experts;
+  rp->job_tokens = kJobTokens;  // the decode path sets its own width below
   rp->ctl = (int*)(b + L.ctl);
   rp->ids = (int*)(b + L.ids);
   rp->wts = (float*)(b + L.wts);
@@ -213,9 +214,11 @@ int prepare_call(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t w
     // with precomputed ids one expert may repeat within a token, so a job can hold up to T*k tokens
     const long long per_job = have_logits ? a->tokens : (long long)a->tokens * a->top_k;
     sp->job_tokens = (int)(per_job < kJobTokens ? per_job : kJobTokens);
-    // the in-kernel router may split jobs finer, so that the shared-memory plan keeps its large stages
-    if (small) sp->job_tokens = skinny_job_cap(s->hidden, s->inter, sp->job_tokens, (int)routes);
+    // jobs may be cut finer, so that the shared-memory plan keeps its large stages and two activation buffers
+    const int per_expert = (int)((routes + s->total_experts - 1) / s->total_experts);  // expected routes per expert
+    sp->job_tokens = skinny_job_cap(s->hidden, s->inter, sp->job_tokens, small ? (int)routes : 0, per_expert);
     if (small && a->tokens == 2 && skinny_two_one_token_jobs(s->hidden, s->inter, (int)routes)) sp->job_tokens = 1;
+    if (!plan->wide) rp->job_tokens = sp->job_tokens;  // the separate router cuts the jobs at the same width
   }
   sp->post_norm = post_norm ? 1 : 0;
   sp->grid_combine = (post_norm || !small) ? 1 : 0;

@@ -11,6 +11,7 @@ struct RouteParams {
   const int* ids_in;       // [T, k] or null
   const float* wts_in;     // [T, k] or null
   int T, k, E_tot, lo, E_loc;
+  int job_tokens;           // decode-path jobs hold at most this many routes (1..kJobTokens)
   int* ctl;
   int* ids;
   float* wts;
@@ -136,7 +137,7 @@ size_t wide_smem_bytes();
 size_t route_smem_bytes(int E_loc);
 int launch_skinny(const SkinnyParams& p, cudaStream_t stream);
 bool skinny_supported(int H, int I);  // the decode kernel has a stage plan for this shape
-int skinny_job_cap(int H, int I, int want, int route_R);
+int skinny_job_cap(int H, int I, int want, int route_R, int min_rows);
 bool skinny_two_one_token_jobs(int H, int I, int route_R);
 int launch_pack(const PackParams& p, cudaStream_t stream);
 int launch_quantize(const QuantParams& p, cudaStream_t stream);

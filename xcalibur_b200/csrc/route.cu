@@ -9,7 +9,7 @@
 //   2. per-expert histogram of local routes (shared-memory atomics), exclusive scan -> offsets;
 //   3. stable permutation: position of flat route f = t*k + s is offsets[e] + #{f' < f : id[f'] = e}, computed
 //      1024 routes at a time with __match_any_sync ranks and a per-warp prefix (bit-exact with a stable sort);
-//   4. the decode-path job list: each expert's routes cut into jobs of at most kJobTokens tokens.
+//   4. the decode-path job list: each expert's routes cut into jobs of at most p.job_tokens tokens.
 // Above kChunkedRouteMin routes the same steps run as three multi-CTA kernels (below).
 #include "common.cuh"
 #include "kernels.cuh"
@@ -69,7 +69,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(RouteParams p) 
   // ---- 2. offsets and jobs
   for (int e = tid; e < p.E_loc; e += kRouteThreads) {
     base[e] = cnt[e];
-    jcnt[e] = (cnt[e] + kJobTokens - 1) / kJobTokens;
+    jcnt[e] = (cnt[e] + p.job_tokens - 1) / p.job_tokens;
   }
   __syncthreads();
   if (warp == 0) {
@@ -86,8 +86,8 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(RouteParams p) 
     p.offsets[e] = base[e];
     const int c = cnt[e];
     int j = jcnt[e];
-    for (int s0 = 0; s0 < c; s0 += kJobTokens, ++j) {
-      p.jobs[j] = make_int4(e, base[e] + s0, min(kJobTokens, c - s0), 0);
+    for (int s0 = 0; s0 < c; s0 += p.job_tokens, ++j) {
+      p.jobs[j] = make_int4(e, base[e] + s0, min(p.job_tokens, c - s0), 0);
       p.doneA[j] = 0;
     }
   }
@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_scan_kernel(RouteParam
       run += v;
     }
     base[e] = run;
-    jcnt[e] = (run + kJobTokens - 1) / kJobTokens;
+    jcnt[e] = (run + p.job_tokens - 1) / p.job_tokens;
   }
   __syncthreads();
   if (warp == 0) {
@@ -223,8 +223,8 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_scan_kernel(RouteParam
     p.counts[e] = c;
     p.offsets[e] = b0;
     int j = jcnt[e];
-    for (int s0 = 0; s0 < c; s0 += kJobTokens, ++j) {
-      p.jobs[j] = make_int4(e, b0 + s0, min(kJobTokens, c - s0), 0);
+    for (int s0 = 0; s0 < c; s0 += p.job_tokens, ++j) {
+      p.jobs[j] = make_int4(e, b0 + s0, min(p.job_tokens, c - s0), 0);
       p.doneA[j] = 0;
     }
   }

@@ -1138,18 +1138,26 @@ int skinny_config(int* grid_out, SkLayout* plan, int H, int I, int job_tokens, i
   return XCB_OK;
 }
 
-// Tokens per job for the in-kernel router: the most (up to `want`) whose shared-memory plan keeps the stage sizes
-// of the one-token plan, so that batches of a few tokens do not fall back to small copies, and its two activation
-// buffers (with one, a segment's rows are staged while no other segment computes).  At the reference's shape
-// (H = I = 4096) this gives 6-token jobs with two buffers rather than 8-token jobs with one: 91 -> 83 us at 8 tokens,
-// 126 -> 117 us at 16.
-int skinny_job_cap(int H, int I, int want, int route_R) {
+// Tokens per job for the decode path: the most (up to `want`) whose shared-memory plan keeps the stage sizes of the
+// one-token plan, so that batches of a few tokens do not fall back to small copies, and also its two activation
+// buffers (with one, a segment's rows are staged while no other segment computes) as long as that width still
+// holds `min_rows` routes, the expected routes per expert (narrower jobs would stream an expert's weights once per
+// job).  At the reference's shape (H = I = 4096) this gives 6-token jobs with two buffers rather than 8-token jobs
+// with one: 91 -> 83 us at 8 tokens, 126 -> 117 us at 16.
+int skinny_job_cap(int H, int I, int want, int route_R, int min_rows) {
   const SkLayout one = sk_layout(H, I, 1, route_R);
+  int same_stages = 1;
+  bool found = false;
   for (int r = want < kJobTokens ? want : kJobTokens; r > 1; --r) {
     const SkLayout L = sk_layout(H, I, r, route_R);
-    if (L.nstage >= 3 && L.perA == one.perA && L.perB == one.perB && L.nbuf >= one.nbuf) return r;
+    if (L.nstage < 3 || L.perA != one.perA || L.perB != one.perB) continue;
+    if (!found) {
+      same_stages = r;
+      found = true;
+    }
+    if (L.nbuf >= one.nbuf) return r >= min_rows ? r : same_stages;
   }
-  return 1;
+  return 1 >= min_rows ? 1 : same_stages;  // one-token jobs keep the one-token plan itself
 }
 
 // Two tokens: one-token jobs are worth an expert the tokens share being streamed twice when they keep two activation

@@ -46,8 +46,8 @@ inline WsLayout ws_layout(int E_loc, int H, int I, int max_tokens, int top_k) {
   WsLayout L;
   const size_t R = (size_t)max_tokens * (size_t)top_k;
   L.max_routes = (int)R;
-  const size_t ej = (size_t)E_loc < R ? (size_t)E_loc : R;
-  L.max_jobs = (int)(R / kJobTokens + ej + 1);
+  // every job holds at least one route, and the in-kernel router may cut jobs as narrow as one route
+  L.max_jobs = (int)(R + 1);
   size_t o = 0;
   auto take = [&](size_t bytes) {
     size_t at = o;
