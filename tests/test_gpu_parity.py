@@ -269,6 +269,24 @@ def test_deepseek_decode_two_tokens(dev, source):
     assert_close_bf16(out, oracle_layer(x, weights, want_ids, want_w))
 
 
+def test_many_one_route_jobs_on_a_small_shard(dev):
+    """At the C2 hidden size the decode path cuts one-route jobs.  A shard of 8 local experts out of 64, with 32
+    tokens that all route to those 8, gives 256 jobs: the workspace's per-job counters must hold one job per route
+    (a bound of routes / 8 + local experts would hold 41), and the output must match the oracle."""
+    from xcalibur_b200 import PreparedMoE
+
+    weights, x, _ = _synthetic(8, 7168, 2048, 32, 140, dev)
+    layer = PreparedMoE(*weights.values(), total_experts=64, expert_offset=0)
+    rng = np.random.default_rng(141)
+    ids = np.stack([rng.permutation(8) for _ in range(32)]).astype(np.int32)
+    wts = rng.dirichlet(np.ones(8), size=32).astype(np.float32)
+    out = layer.forward(x, None, topk_ids=torch.from_numpy(ids).to(dev), topk_weights=torch.from_numpy(wts).to(dev),
+                        path="decode")
+    torch.cuda.synchronize()
+    assert layer.check_device_status() == 0
+    assert_close_bf16(out, oracle_layer(x, weights, ids, wts))
+
+
 @pytest.mark.parametrize("T", [1, 8, 64, 512])
 def test_qwen3_parity(dev, T):
     """C4 shape (H=2048, I=768, E=128, top-8)."""
