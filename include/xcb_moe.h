@@ -121,6 +121,16 @@ size_t xcb_moe_workspace_bytes(const XcbMoeShape* shape, int32_t max_tokens, int
  * Returns the number of entries written (6) or -1 on bad arguments. */
 int xcb_moe_workspace_offsets(const XcbMoeShape* shape, int32_t max_tokens, int32_t top_k, size_t* out, int n);
 
+/* How a forward call of this shape and size would run, without touching the GPU (a diagnostic, for tests and for
+ * callers sizing their batches; no counterpart in the reference, whose kernel_fn picks a build by token count,
+ * moe_w4a16.py:3384-3393).  given_routes: 1 for topk_ids/topk_weights, 0 for router logits.  out[0] path (0 decode,
+ * 1 prefill), out[1] routes computed inside the decode kernel (1) or by the router kernel (0), out[2] routes per
+ * decode job, out[3] activation rows per buffer, out[4] activation buffers, out[5] weight-ring stages, out[6] bytes
+ * per stage, out[7] the decode kernel stages both rows of a two-token call at start (1).  Decode fields are 0 on
+ * the prefill path.  Returns the number of entries written (8, or n if smaller) or an XCB_ERR_* code. */
+int xcb_moe_plan_info(const XcbMoeShape* shape, int32_t tokens, int32_t top_k, int32_t flags, int32_t given_routes,
+                      int32_t* out, int32_t n);
+
 /* Zero a fresh workspace (once, before its first forward call).  Calls keep it consistent afterwards. */
 int xcb_moe_workspace_init(void* workspace, size_t bytes, int32_t max_tokens, int32_t top_k, cudaStream_t stream);
 

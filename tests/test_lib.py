@@ -74,3 +74,58 @@ def test_forward_rejects_bad_arguments_before_launch():
     assert lib.xcb_moe_forward(ctypes.byref(w), ctypes.byref(a), 16, 1 << 30, None) == _lib.XCB_ERR_INVALID_ARG
     a = _lib.XcbMoeArgs(0, 2, 0, 0, 16, 16, None, None, 16, None, None)      # T = 0: nothing to do
     assert lib.xcb_moe_forward(ctypes.byref(w), ctypes.byref(a), 16, 0, None) == _lib.XCB_OK
+
+
+def _plan(shape, T, k, given, flags=0):
+    """xcb_moe_plan_info: the planner of a forward call, run without a GPU."""
+    lib = _lib.load()
+    out = (ctypes.c_int32 * 8)()
+    assert lib.xcb_moe_plan_info(ctypes.byref(shape), T, k, flags, int(given), out, 8) == 8
+    keys = ("prefill", "in_kernel_routes", "job_routes", "rows", "buffers", "stages", "stage_bytes", "two_token")
+    return dict(zip(keys, list(out)))
+
+
+def test_plan_of_the_deepseek_decode_step():
+    """Configuration 2 (one token, router logits): one launch, one-route jobs, two activation buffers and the three
+    64.5 KB stages of the one-token plan."""
+    p = _plan(_shape(256, H=7168, I=2048), 1, 8, False)
+    assert p == {"prefill": 0, "in_kernel_routes": 1, "job_routes": 1, "rows": 1, "buffers": 2, "stages": 3,
+                 "stage_bytes": 64512, "two_token": 0}
+
+
+def test_plan_of_two_tokens_stages_both_rows():
+    """Two tokens at the DeepSeek-V3 shape: one-token jobs keep two buffers, and the kernel instantiation that
+    stages both rows at start runs (routes given, as the expert-parallel local layer passes them)."""
+    p = _plan(_shape(128, Et=256, H=7168, I=2048), 2, 8, True)
+    assert (p["prefill"], p["job_routes"], p["rows"], p["buffers"], p["two_token"]) == (0, 1, 1, 2, 1)
+
+
+@pytest.mark.parametrize("T", [1, 8, 16, 32, 128])
+def test_plan_at_the_reference_shape_keeps_two_buffers(T):
+    """The reference's shape (H = I = 4096, 32 of 256 experts, given routes): the decode path with jobs as wide as
+    two activation buffers allow (not 8-route jobs with one buffer and three stages)."""
+    p = _plan(_shape(32, Et=256, H=4096, I=4096), T, 8, True)
+    assert p["prefill"] == 0 and p["buffers"] == 2 and p["stage_bytes"] == 36864
+    assert 1 <= p["job_routes"] <= 8 and p["rows"] == p["job_routes"]
+    assert p["in_kernel_routes"] == int(T * 8 <= 256)
+
+
+def test_plan_keeps_wide_jobs_when_experts_get_many_routes():
+    """When the expected routes per expert exceed what two buffers allow, the jobs stay wide: narrower jobs would
+    stream an expert's weights once per job."""
+    p = _plan(_shape(256, H=7168, I=2048), 64, 8, False, flags=_lib.XCB_FLAG_DECODE_PATH)
+    assert p["prefill"] == 0 and p["in_kernel_routes"] == 0 and p["job_routes"] >= 2
+
+
+def test_plan_of_a_large_batch_is_the_prefill_path():
+    p = _plan(_shape(256, H=7168, I=2048), 4096, 8, False)
+    assert p["prefill"] == 1 and p["job_routes"] == 0
+
+
+def test_plan_info_rejects_bad_arguments():
+    lib = _lib.load()
+    out = (ctypes.c_int32 * 8)()
+    s = _shape()
+    assert lib.xcb_moe_plan_info(ctypes.byref(s), 0, 8, 0, 0, out, 8) == _lib.XCB_ERR_INVALID_ARG
+    assert lib.xcb_moe_plan_info(ctypes.byref(s), 4, 17, 0, 0, out, 8) == _lib.XCB_ERR_INVALID_ARG
+    assert lib.xcb_moe_plan_info(ctypes.byref(_shape(E=0)), 4, 8, 0, 0, out, 8) != 8

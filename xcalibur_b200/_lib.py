@@ -39,6 +39,7 @@ EXPORTS = (
     "xcb_moe_pack_weights",
     "xcb_moe_workspace_bytes",
     "xcb_moe_workspace_offsets",
+    "xcb_moe_plan_info",
     "xcb_moe_workspace_init",
     "xcb_moe_forward",
     "xcb_moe_route",
@@ -99,6 +100,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         "xcb_moe_workspace_bytes": (SZ, [ctypes.POINTER(XcbMoeShape), I32, I32]),
         "xcb_moe_workspace_offsets": (ctypes.c_int, [ctypes.POINTER(XcbMoeShape), I32, I32,
                                                       ctypes.POINTER(ctypes.c_size_t), ctypes.c_int]),
+        "xcb_moe_plan_info": (ctypes.c_int, [ctypes.POINTER(XcbMoeShape), I32, I32, I32, I32,
+                                              ctypes.POINTER(ctypes.c_int32), I32]),
         "xcb_moe_workspace_init": (ctypes.c_int, [P, SZ, I32, I32, P]),
         "xcb_moe_forward": (ctypes.c_int, [ctypes.POINTER(XcbMoeWeights), ctypes.POINTER(XcbMoeArgs), P, SZ, P]),
         "xcb_moe_route": (ctypes.c_int, [ctypes.POINTER(XcbMoeWeights), ctypes.POINTER(XcbMoeArgs), P, SZ, P]),

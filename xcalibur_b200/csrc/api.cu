@@ -266,6 +266,47 @@ int run_experts(const CallPlan& plan, cudaStream_t stream) {
 }
 }  // namespace
 
+// The planner of a forward call (prepare_call, unchanged), run on placeholder pointers: it only checks them for
+// null and alignment, and nothing here reads or launches anything.
+int xcb_moe_plan_info(const XcbMoeShape* shape, int32_t tokens, int32_t top_k, int32_t flags, int32_t given_routes,
+                      int32_t* out, int32_t n) {
+  if (!shape || !out || n <= 0 || tokens <= 0) return XCB_ERR_INVALID_ARG;
+  int rc = shape_ok(shape);
+  if (rc != XCB_OK) return rc;
+  const uintptr_t fake = 256;  // 16-byte aligned, never dereferenced
+  XcbMoeWeights w{};
+  w.shape = *shape;
+  w.gate_up = w.down = (const void*)fake;
+  w.gate_up_gs = w.down_gs = (const float*)fake;
+  w.post_norm_w = (flags & XCB_FLAG_POST_NORM) ? (const uint16_t*)fake : nullptr;
+  XcbMoeArgs a{};
+  a.tokens = tokens;
+  a.top_k = top_k;
+  a.flags = flags & ~XCB_FLAG_PDL;
+  a.hidden_states = (const uint16_t*)fake;
+  a.out = (uint16_t*)fake;
+  if (given_routes) {
+    a.topk_ids = (const int32_t*)fake;
+    a.topk_weights = (const float*)fake;
+  } else {
+    a.router_logits = (const float*)fake;
+  }
+  if (top_k <= 0 || top_k > 16) return XCB_ERR_INVALID_ARG;
+  CallPlan plan;
+  rc = prepare_call(&w, &a, (void*)fake, xcb_moe_workspace_bytes(shape, tokens, top_k), &plan);
+  if (rc != XCB_OK) return rc;
+  int v[8] = {plan.wide ? 1 : 0, 0, 0, 0, 0, 0, 0, 0};
+  if (!plan.wide) {
+    v[1] = plan.sp.small_route;
+    v[2] = plan.sp.job_tokens;
+    skinny_plan_fields(shape->hidden, shape->inter, plan.sp.job_tokens, plan.sp.small_route ? tokens * top_k : 0,
+                       tokens, v + 3);
+  }
+  const int m = n < 8 ? n : 8;
+  for (int i = 0; i < m; ++i) out[i] = v[i];
+  return m;
+}
+
 int xcb_moe_route(const XcbMoeWeights* w, const XcbMoeArgs* a, void* ws, size_t ws_bytes, cudaStream_t stream) {
   CallPlan plan;
   int rc = prepare_call(w, a, ws, ws_bytes, &plan);

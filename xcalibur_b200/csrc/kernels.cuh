@@ -139,6 +139,8 @@ int launch_skinny(const SkinnyParams& p, cudaStream_t stream);
 bool skinny_supported(int H, int I);  // the decode kernel has a stage plan for this shape
 int skinny_job_cap(int H, int I, int want, int route_R, int min_rows);
 bool skinny_two_one_token_jobs(int H, int I, int route_R);
+// rows, buffers, stages, stage bytes and the two-token instantiation flag of the decode kernel's plan
+void skinny_plan_fields(int H, int I, int job_tokens, int route_R, int T, int* out);
 int launch_pack(const PackParams& p, cudaStream_t stream);
 int launch_quantize(const QuantParams& p, cudaStream_t stream);
 

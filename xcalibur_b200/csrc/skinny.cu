@@ -1167,6 +1167,15 @@ bool skinny_two_one_token_jobs(int H, int I, int route_R) {
   return one.nstage >= 3 && one.nbuf == 2 && (two.nstage < 3 || two.nbuf < 2);
 }
 
+void skinny_plan_fields(int H, int I, int job_tokens, int route_R, int T, int* out) {
+  const SkLayout L = sk_layout(H, I, job_tokens, route_R);
+  out[0] = L.rows;
+  out[1] = L.nbuf;
+  out[2] = L.nstage;
+  out[3] = L.slot_bytes;
+  out[4] = T == 2 && L.rows == 1 && L.nbuf == 2 ? 1 : 0;  // launch_skinny's choice of instantiation
+}
+
 bool skinny_supported(int H, int I) {
   return sk_layout(H, I, kJobTokens, kSmallRoutes).nstage >= 3 && sk_layout(H, I, 1, kSmallRoutes).nstage >= 3;
 }
