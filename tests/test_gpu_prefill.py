@@ -261,6 +261,21 @@ def _full_size_check(dev, E, H, I, T, k, seed, bias_std):
     return want_ids, rows
 
 
+@pytest.mark.parametrize("T", [64, 96])
+def test_deepseek_v3_mid_batch_on_the_decode_path(dev, T):
+    """64 and 96 tokens at the DeepSeek-V3 shape (up to 3 routes per expert): the library takes the decode path with
+    the separate router; ids and weights of every route exact, 32 sampled rows against the oracle."""
+    import ctypes
+
+    from xcalibur_b200 import _lib
+
+    shape = _lib.XcbMoeShape(256, 256, 0, 7168, 2048)
+    out = (ctypes.c_int32 * 8)()
+    assert _lib.load().xcb_moe_plan_info(ctypes.byref(shape), T, 8, 0, 0, out, 8) == 8
+    assert out[0] == 0 and out[1] == 0  # decode path, routes from the router kernel
+    _full_size_check(dev, 256, 7168, 2048, T, 8, 320 + T, 0.0)
+
+
 def test_prefill_deepseek_v3_t4096_sampled_rows(dev):
     """Configuration 3 at its full size (T = 4096, DeepSeek-V3 shape, router bias N(0, 0.5)): ids and weights of
     all 32768 routes bit-exact, and 32 rows (on the hottest and the coldest experts, and rows sharing experts)

@@ -129,3 +129,10 @@ def test_plan_info_rejects_bad_arguments():
     assert lib.xcb_moe_plan_info(ctypes.byref(s), 0, 8, 0, 0, out, 8) == _lib.XCB_ERR_INVALID_ARG
     assert lib.xcb_moe_plan_info(ctypes.byref(s), 4, 17, 0, 0, out, 8) == _lib.XCB_ERR_INVALID_ARG
     assert lib.xcb_moe_plan_info(ctypes.byref(_shape(E=0)), 4, 8, 0, 0, out, 8) != 8
+
+
+@pytest.mark.parametrize("T,prefill", [(32, 0), (48, 0), (96, 0), (97, 1), (128, 1)])
+def test_plan_path_by_routes_per_expert(T, prefill):
+    """A layer holding all 256 DeepSeek-V3 experts stays on the decode path up to 3 routes per expert on average
+    (96 tokens x top-8), where its weight stream beats the tensor-core path."""
+    assert _plan(_shape(256, H=7168, I=2048), T, 8, False)["prefill"] == prefill
