@@ -136,3 +136,16 @@ def test_plan_path_by_routes_per_expert(T, prefill):
     """A layer holding all 256 DeepSeek-V3 experts stays on the decode path up to 3 routes per expert on average
     (96 tokens x top-8), where its weight stream beats the tensor-core path."""
     assert _plan(_shape(256, H=7168, I=2048), T, 8, False)["prefill"] == prefill
+
+
+@pytest.mark.parametrize("T,prefill", [(32, 0), (48, 0), (49, 1), (64, 1)])
+def test_plan_path_at_the_qwen3_shape(T, prefill):
+    """128 experts (H = 2048, I = 768): 3 routes per expert is 48 tokens x top-8."""
+    assert _plan(_shape(128, H=2048, I=768), T, 8, False)["prefill"] == prefill
+
+
+def test_plan_shard_path_uses_the_held_routes():
+    """An expert-parallel shard (32 of 256 experts held) is planned by the routes it expects to hold: 128 tokens x
+    top-8 (~128 held routes) decode, 256 tokens (~256) prefill."""
+    assert _plan(_shape(32, Et=256, H=4096, I=4096), 128, 8, True)["prefill"] == 0
+    assert _plan(_shape(32, Et=256, H=4096, I=4096), 256, 8, True)["prefill"] == 1
